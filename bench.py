@@ -1,0 +1,502 @@
+#!/usr/bin/env python
+"""Decode-attention benchmark (one JSON line on rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload cfg2|cfg3|cfg4]
+
+Default workload (cfg2, the configuration the headline metric is quoted on):
+Qwen2-1.5B-shaped decode attention, batch 1, 12 query heads, 2 KV heads,
+head_dim 128, over all 28 layers of a contiguous fp16 cache
+[28 x 2 x 16384 x 2 x 128] (470 MB, N(0,1) synthetic data), once at each
+kv_len in {512, 2048, 4096, 16384}.  One step = those 4 x 28 = 112
+decode_attn_v4_flash-equivalent calls (fr_decode_attn).  Each kv_len group
+is one CUDA graph of 28 calls; L2 is flushed (256 MiB write) before every
+group and the CUDA events bracket only the group, so every K/V byte comes
+from HBM.  metric = algorithmic bytes (K+V of the valid range + q + out)
+per second.
+
+With N > 1 (torchrun) every rank decodes its own sequence (its own cache,
+seeded by rank): batched decode sharded by sequence, no collective on the
+data path; value = all ranks' bytes / the slowest rank's time ("weak").
+
+--workload cfg3 (batched ragged, 64 sequences x 4 kv heads sharded by
+(sequence, kv head) across ranks, "strong") and cfg4 (one 128K-token
+sequence, KV range split across ranks, NCCL all-gather of the per-rank
+(m, l, acc) states + LSE merge, "strong") measure the multi-GPU paths.
+
+--impl reference times the reference's own CPU implementation
+(cpu_decode_attn, tests/test_kernels.cpp:229-270, compiled from the
+reference sources into oracle/_ref) on the same workload with all host
+threads; rank 0 alone runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from forgert_b200 import workloads as W  # noqa: E402
+
+METRIC = "decode-attn HBM GB/s (algorithmic K+V+q+out bytes / s)"
+UNIT = "GB/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2")
+    ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of graphs")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu", action="store_true",
+                    help="profiling run: few steps, no clocks/e2e/cpu legs")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def emit(obj) -> None:
+    print(json.dumps(obj), flush=True)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_per_launch():
+    """DRAM bytes per launch of the dominant kernel from a committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text())
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------ clock sampler
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML every few ms."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int, period_s: float = 0.005):
+        self.samples = []
+        self.period = period_s
+        self.stop_ev = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.nvml = None
+        self.t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        n = self.nvml
+        while not self.stop_ev.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
+                rs = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, rs))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop_ev.set()
+        if self.ok:
+            self.t.join(timeout=2)
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return None
+        mhz = [s[0] for s in self.samples]
+        mask = 0
+        for _, r in self.samples:
+            mask |= int(r)
+        reasons = [name for bit, name in self.REASONS.items() if mask & bit and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(mhz)}
+
+
+# --------------------------------------------------------------- our arm
+class Cfg2:
+    """28 layers x kv_len {512, 2048, 4096, 16384}, one sequence per rank."""
+
+    L, S, H, HKV, D = W.CFG2_LAYERS, W.CFG2_MAX_SEQ, 12, 2, 128
+
+    def __init__(self, torch, rank: int, device):
+        self.torch = torch
+        g = torch.Generator(device=device)
+        g.manual_seed(1 + 1000 * rank)
+        self.cache = torch.empty((self.L, 2, self.S, self.HKV, self.D), dtype=torch.float16,
+                                 device=device)
+        self.cache.normal_(generator=g)
+        self.q = torch.empty((self.L, self.H, self.D), dtype=torch.float16, device=device)
+        self.q.normal_(generator=g)
+        self.out = torch.empty_like(self.q)
+        self.groups = list(W.CFG2_KV_LENS)
+        self.q_host = self.q.cpu().pin_memory()
+        self.out_host = torch.empty_like(self.q_host).pin_memory()
+
+    def bytes_per_group(self, kv: int) -> int:
+        return self.L * W.decode_bytes([kv], self.H, self.HKV, self.D)
+
+    def bytes_per_step(self) -> int:
+        return sum(self.bytes_per_group(kv) for kv in self.groups)
+
+    def calls_per_group(self) -> int:
+        return self.L
+
+    def workspace_bytes(self, A) -> int:
+        return max(A.decode_workspace_size(1, self.H, self.HKV, self.D, kv) for kv in self.groups)
+
+    def run_group(self, A, kv: int, stream) -> None:
+        for l in range(self.L):
+            A.decode_attn_v4_flash(self.q[l], self.cache[l, 0], self.cache[l, 1], self.out[l],
+                                   self.H, self.HKV, self.D, kv, stream)
+
+    def run_group_e2e(self, A, kv: int, stream) -> None:
+        for l in range(self.L):
+            self.q[l].copy_(self.q_host[l], non_blocking=True)
+            A.decode_attn_v4_flash(self.q[l], self.cache[l, 0], self.cache[l, 1], self.out[l],
+                                   self.H, self.HKV, self.D, kv, stream)
+            self.out_host[l].copy_(self.out[l], non_blocking=True)
+
+    def e2e_bytes(self):
+        per = self.H * self.D * 2
+        n = self.L * len(self.groups)
+        return n * per, n * per
+
+    def config(self):
+        return {
+            "workload": "cfg2: Qwen2-1.5B-shape decode attention, batch 1 per GPU, "
+                        "28 layers x kv_len {512, 2048, 4096, 16384}",
+            "model": "Qwen2-1.5B attention shape (random data)",
+            "batch_per_gpu": 1, "num_heads": self.H, "num_kv_heads": self.HKV,
+            "head_dim": self.D, "layers": self.L, "kv_lens": self.groups,
+            "cache": "contiguous fp16 [28 x 2 x 16384 x 2 x 128] per GPU",
+            "l2": "flushed (256 MiB write) before each kv_len group; events exclude the flush",
+        }
+
+
+def run_ours(args, torch, dist, rank, local_rank, world):
+    from forgert_b200 import attention as A
+    from forgert_b200 import _lib
+
+    lib = _lib.load()
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if args.workload != "cfg2":
+        raise SystemExit(f"workload {args.workload} not implemented yet")
+    wl = Cfg2(torch, rank, device)
+    stream = torch.cuda.Stream(device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    A.reserve_workspace(wl.workspace_bytes(A))
+    torch.cuda.synchronize()
+
+    # Eager warm-up (creates the library's device state outside capture).
+    with torch.cuda.stream(stream):
+        for kv in wl.groups:
+            wl.run_group(A, kv, stream)
+    torch.cuda.synchronize()
+
+    use_graph = not args.no_graph
+    graphs = {}
+    launches_per_step = 0
+    if use_graph:
+        for kv in wl.groups:
+            g = torch.cuda.CUDAGraph()
+            c0 = lib.fr_launch_count()
+            with torch.cuda.graph(g, stream=stream):
+                wl.run_group(A, kv, torch.cuda.current_stream())
+            launches_per_step += lib.fr_launch_count() - c0
+            graphs[kv] = g
+    else:
+        c0 = lib.fr_launch_count()
+        with torch.cuda.stream(stream):
+            for kv in wl.groups:
+                wl.run_group(A, kv, stream)
+        torch.cuda.synchronize()
+        launches_per_step = lib.fr_launch_count() - c0
+
+    def step(events):
+        for i, kv in enumerate(wl.groups):
+            flush.fill_(i & 0xFF)
+            if events is not None:
+                events[i][0].record(stream)
+            if use_graph:
+                graphs[kv].replay()
+            else:
+                wl.run_group(A, kv, stream)
+            if events is not None:
+                events[i][1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step(None)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    K = args.steps
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in wl.groups]
+          for _ in range(K)]
+    sampler = ClockSampler(local_rank) if not args.ncu else None
+    if sampler:
+        sampler.__enter__()
+    with torch.cuda.stream(stream):
+        for k in range(K):
+            step(ev[k])
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.__exit__()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    group_ms = {kv: sum(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(K))
+                for i, kv in enumerate(wl.groups)}
+    total_ms = sum(group_ms.values())
+    assert A.device_error() == 0, "in-kernel wait timed out"
+    max_ms = total_ms
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        max_ms = float(t.item())
+    total_bytes = wl.bytes_per_step() * K * world
+    value = total_bytes / (max_ms * 1e-3) / 1e9
+
+    # ---- end to end through the C ABI with pinned host buffers (eager calls)
+    e2e = None
+    if not args.ncu:
+        Ke = max(3, min(K, 200))
+        ev2 = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in wl.groups]
+               for _ in range(Ke)]
+        with torch.cuda.stream(stream):
+            for kv in wl.groups:
+                wl.run_group_e2e(A, kv, stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        with torch.cuda.stream(stream):
+            for k in range(Ke):
+                for i, kv in enumerate(wl.groups):
+                    flush.fill_(i & 0xFF)
+                    ev2[k][i][0].record(stream)
+                    wl.run_group_e2e(A, kv, stream)
+                    ev2[k][i][1].record(stream)
+        torch.cuda.synchronize()
+        e_ms = sum(ev2[k][i][0].elapsed_time(ev2[k][i][1]) for k in range(Ke)
+                   for i in range(len(wl.groups)))
+        if world > 1:
+            t = torch.tensor([e_ms], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        h2d, d2h = wl.e2e_bytes()
+        e2e = {"value": wl.bytes_per_step() * Ke * world / (e_ms * 1e-3) / 1e9, "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "how": "per call: H2D q from pinned host, fr_decode_attn, D2H out to pinned host; "
+                      "eager launches, CUDA events, L2 flushed per kv_len group"}
+
+    if rank != 0:
+        return
+    peak, peak_kind = peaks()
+    sweep = {}
+    for kv in wl.groups:
+        us = group_ms[kv] * 1e3 / (K * wl.calls_per_group())
+        gbs = W.decode_bytes([kv], wl.H, wl.HKV, wl.D) / (us * 1e-6) / 1e9
+        sweep[str(kv)] = {"us_per_call": round(us, 3), "gbs": round(gbs, 1),
+                          "frac_of_measured_hbm": round(gbs / peak, 4)}
+    dom = str(max(wl.groups))
+    tr = traffic_per_launch()
+    roofline = {
+        "bound": "hbm", "kernel": "split_decode_kernel + lse_merge_kernel (one fr_decode_attn "
+                                  f"call, kv_len {dom})",
+        "achieved": sweep[dom]["gbs"], "peak": peak, "unit": "GB/s",
+        "frac": round(sweep[dom]["gbs"] / peak, 4), "peak_kind": peak_kind,
+        "traffic": tr.get("dram_bytes_per_launch") if tr else None,
+        "algorithmic_bytes_per_launch": W.decode_bytes([int(dom)], wl.H, wl.HKV, wl.D),
+    }
+    cfg = wl.config()
+    cfg.update({"parallelism": f"dp{world} (one sequence per GPU)", "graph": use_graph,
+                "sweep": sweep})
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(max_ms / K, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+        "data": "synthetic N(0,1) fp16", "config": cfg, "roofline": roofline,
+        "gpu_launches": int(launches_per_step * K), "e2e": e2e,
+        "clocks": sampler.summary() if sampler else None,
+    }
+    if world == 1 and not args.no_cpu_baseline and not args.ncu:
+        line["cpu_baseline"] = cpu_baseline_cfg2(budget_s=12.0)
+    emit(line)
+
+
+# --------------------------------------------------------- reference arm
+def _cfg2_host_problem(layers):
+    """fp32 copies of cfg2 layers (K, V [16384, 2, 128]) and q per layer."""
+    data = []
+    for l in layers:
+        k, v = W.cfg2_layer_kv(l)
+        q = W.cfg2_layer_q(l)
+        data.append((np.ascontiguousarray(q, np.float32), np.ascontiguousarray(k, np.float32),
+                     np.ascontiguousarray(v, np.float32)))
+    return data
+
+
+class _RefRunner:
+    """cpu_decode_attn calls over all host threads (oracle/_ref), else the C port."""
+
+    def __init__(self, data, kv_lens):
+        from oracle import oracle as O
+
+        self.O = O
+        self.lib = O.load_ref()
+        self.kind = "reference" if self.lib is not None else "port"
+        self.threads = os.cpu_count() or 1
+        self.calls = [(q, k, v, kv) for kv in kv_lens for (q, k, v) in data]
+        self.outs = [np.zeros((12, 128), np.float32) for _ in self.calls]
+        f32p = ctypes.POINTER(ctypes.c_float)
+        n = len(self.calls)
+        if self.lib is not None:
+            self.qs = (f32p * n)(*[q.ctypes.data_as(f32p) for q, _, _, _ in self.calls])
+            self.ks = (f32p * n)(*[k.ctypes.data_as(f32p) for _, k, _, _ in self.calls])
+            self.vs = (f32p * n)(*[v.ctypes.data_as(f32p) for _, _, v, _ in self.calls])
+            self.os_ = (f32p * n)(*[o.ctypes.data_as(f32p) for o in self.outs])
+            self.lens = (ctypes.c_int * n)(*[kv for _, _, _, kv in self.calls])
+
+    def run(self):
+        if self.lib is not None:
+            self.lib.ref_cpu_decode_attn_many(self.qs, self.ks, self.vs, self.os_, self.lens,
+                                              len(self.calls), 12, 2, 128, self.threads)
+            return
+        from concurrent.futures import ThreadPoolExecutor
+        lib = self.O.load_oracle()
+        f32p = ctypes.POINTER(ctypes.c_float)
+
+        def one(i):
+            q, k, v, kv = self.calls[i]
+            lib.oracle_decode_attn_f32(q.ctypes.data_as(f32p), k.ctypes.data_as(f32p),
+                                       v.ctypes.data_as(f32p), self.outs[i].ctypes.data_as(f32p),
+                                       12, 2, 128, kv)
+
+        with ThreadPoolExecutor(self.threads) as ex:
+            list(ex.map(one, range(len(self.calls))))
+
+    def bytes(self):
+        return sum(W.decode_bytes([kv], 12, 2, 128) for _, _, _, kv in self.calls)
+
+
+def cpu_baseline_cfg2(budget_s: float):
+    """Bounded sample: 4 layers x the 4 kv_lens, repeated for about budget_s."""
+    runner = _RefRunner(_cfg2_host_problem(range(4)), W.CFG2_KV_LENS)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        runner.run()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 50:
+            break
+    return {"value": round(runner.bytes() * reps / el / 1e9, 4), "unit": UNIT,
+            "cores": runner.threads, "kind": runner.kind,
+            "sample": f"cfg2 layers 0-3 x kv_len {{512,2048,4096,16384}} (16 calls) x {reps} reps, "
+                      f"{el:.1f} s; cpu_decode_attn (tests/test_kernels.cpp:229-270) on "
+                      f"{runner.threads} threads"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    if args.workload != "cfg2":
+        emit({"impl": "reference", "unavailable": f"reference arm implemented for cfg2 only"})
+        return
+    runner = _RefRunner(_cfg2_host_problem(range(W.CFG2_LAYERS)), W.CFG2_KV_LENS)
+    for _ in range(args.warmup):
+        runner.run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        runner.run()
+    el = time.perf_counter() - t0
+    value = runner.bytes() * args.steps / el / 1e9
+    emit({
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el * 1e3 / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 (fp16-valued inputs)", "data": "synthetic N(0,1) fp16",
+        "impl": "reference",
+        "config": {"workload": "cfg2: Qwen2-1.5B-shape decode attention, batch 1, 28 layers x "
+                               "kv_len {512, 2048, 4096, 16384}",
+                   "num_heads": 12, "num_kv_heads": 2, "head_dim": 128, "layers": 28,
+                   "kv_lens": list(W.CFG2_KV_LENS)},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": runner.threads,
+                         "kind": runner.kind,
+                         "sample": "full cfg2 step (112 cpu_decode_attn calls) per step"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    })
+
+
+def main():
+    args = parse_args()
+    rank, local_rank, world = dist_env()
+    if args.gpus != world and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, torch, dist, rank, local_rank, world)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

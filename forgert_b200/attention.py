@@ -1,0 +1,148 @@
+"""Python mirror of ForgeRT's attention launcher interface (kernels/attention.cuh).
+
+Same names, argument order and meaning as the reference's C++ launchers;
+every call goes straight to libforgert_b200.so through the C ABI of
+include/forgert_attn.h.  Arguments that are device buffers accept either a
+CUDA torch tensor or a raw device pointer (int); `stream` is a
+torch.cuda.Stream, a raw cudaStream_t (int) or None (the legacy default
+stream, as in the reference).  Errors raise ForgeRTError, as the reference's
+CUDA_CHECK raises std::runtime_error.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Sequence
+
+from ._lib import ForgeRTError, check, load
+
+__all__ = [
+    "ForgeRTError", "decode_attn_v4_flash", "decode_attn_v0_naive", "decode_attn_v1_coal",
+    "decode_attn_v2_warp_red", "decode_attn_v3_vec", "prefill_attn_causal",
+    "decode_attn_batched", "decode_attn_partial", "lse_merge", "rope_precompute_tables",
+    "rope_append", "reserve_workspace", "decode_workspace_size", "device_error",
+]
+
+
+def _ptr(x) -> int | None:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    dp = getattr(x, "data_ptr", None)
+    if dp is None:
+        raise TypeError(f"expected a device tensor or pointer, got {type(x).__name__}")
+    if not getattr(x, "is_cuda", True):
+        raise ValueError("tensor must live on a CUDA device")
+    return dp()
+
+
+def _stream(s) -> int | None:
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s
+    return getattr(s, "cuda_stream", None) or getattr(s, "stream_id", None) or s
+
+
+def decode_attn_v4_flash(q, k_cache, v_cache, out, num_heads: int, num_kv_heads: int,
+                         head_dim: int, kv_len: int, stream=None) -> None:
+    """Decode attention for one token (kernels/attention.cuh:65-71).
+
+    q/out [num_heads, head_dim] fp16; k_cache/v_cache one layer's
+    [>= kv_len, num_kv_heads, head_dim] fp16 view of the cache.
+    """
+    lib = load()
+    check("fr_decode_attn", lib.fr_decode_attn(
+        _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), num_heads, num_kv_heads, head_dim,
+        kv_len, _stream(stream)))
+
+
+# The reference keeps its earlier versions under their own names
+# (attention.cuh:29-62); they compute the same function, so they all reach
+# the one B200 kernel.
+decode_attn_v0_naive = decode_attn_v4_flash
+decode_attn_v1_coal = decode_attn_v4_flash
+decode_attn_v2_warp_red = decode_attn_v4_flash
+decode_attn_v3_vec = decode_attn_v4_flash
+
+
+def prefill_attn_causal(q, k, v, out, seq_len: int, num_heads: int, num_kv_heads: int,
+                        head_dim: int, stream=None) -> None:
+    """Causal prefill (kernels/attention.cuh:76-82): q/out [seq_len, H, D],
+    k/v [seq_len, Hkv, D]."""
+    lib = load()
+    check("fr_prefill_attn", lib.fr_prefill_attn(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(out), seq_len, num_heads, num_kv_heads, head_dim,
+        _stream(stream)))
+
+
+def decode_attn_batched(q, k_caches, v_caches, kv_lens, out, batch: int, num_heads: int,
+                        num_kv_heads: int, head_dim: int, max_kv_len: int, stream=None) -> None:
+    """Ragged batch: k_caches/v_caches are device arrays of per-sequence cache
+    bases (int64 tensor or pointer), kv_lens a device int32 array."""
+    lib = load()
+    check("fr_decode_attn_batched", lib.fr_decode_attn_batched(
+        _ptr(q), _ptr(k_caches), _ptr(v_caches), _ptr(kv_lens), _ptr(out), batch, num_heads,
+        num_kv_heads, head_dim, max_kv_len, _stream(stream)))
+
+
+def decode_attn_partial(q, k_cache, v_cache, kv_len: int, state_ml, state_acc, num_heads: int,
+                        num_kv_heads: int, head_dim: int, stream=None) -> None:
+    """(m, l, acc) log-sum-exp state per head over positions [0, kv_len)."""
+    lib = load()
+    check("fr_decode_attn_partial", lib.fr_decode_attn_partial(
+        _ptr(q), _ptr(k_cache), _ptr(v_cache), kv_len, _ptr(state_ml), _ptr(state_acc),
+        num_heads, num_kv_heads, head_dim, _stream(stream)))
+
+
+def lse_merge(states_ml, states_acc, num_states: int, out, num_heads: int, head_dim: int,
+              stream=None) -> None:
+    """Merge state-major stacked states ([S, H, 2] and [S, H, D] fp32) to fp16 out [H, D]."""
+    lib = load()
+    check("fr_lse_merge", lib.fr_lse_merge(
+        _ptr(states_ml), _ptr(states_acc), num_states, _ptr(out), num_heads, head_dim,
+        _stream(stream)))
+
+
+def rope_precompute_tables(max_seq_len: int, head_dim: int, base: float, scale: float = 1.0,
+                           device=None):
+    """cos/sin tables [max_seq_len, head_dim/2] fp32 on the device
+    (kernels/rope.cuh:227-231); returns (cos, sin) torch tensors."""
+    import torch
+
+    lib = load()
+    dev = torch.device("cuda") if device is None else torch.device(device)
+    cos = torch.empty((max_seq_len, head_dim // 2), dtype=torch.float32, device=dev)
+    sin = torch.empty_like(cos)
+    with torch.cuda.device(dev):
+        check("fr_rope_tables", lib.fr_rope_tables(
+            cos.data_ptr(), sin.data_ptr(), max_seq_len, head_dim, float(base), float(scale)))
+    return cos, sin
+
+
+def rope_append(q, k, v, k_cache, v_cache, cos_tab, sin_tab, seq_len: int, num_heads: int,
+                num_kv_heads: int, head_dim: int, pos_offset: int, stream=None) -> None:
+    """RoPE on q/k in place + KV append at rows pos_offset.. (one launch)."""
+    lib = load()
+    check("fr_rope_append", lib.fr_rope_append(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), _ptr(cos_tab), _ptr(sin_tab),
+        seq_len, num_heads, num_kv_heads, head_dim, pos_offset, _stream(stream)))
+
+
+def reserve_workspace(nbytes: int) -> None:
+    lib = load()
+    check("fr_reserve_workspace", lib.fr_reserve_workspace(nbytes))
+
+
+def decode_workspace_size(batch: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                          max_kv_len: int) -> int:
+    return int(load().fr_decode_workspace_size(batch, num_heads, num_kv_heads, head_dim,
+                                               max_kv_len))
+
+
+def device_error(clear: bool = True) -> int:
+    """In-kernel error word of the current device (0 = none); synchronises."""
+    lib = load()
+    code = ctypes.c_int(0)
+    lib.fr_get_device_error(1 if clear else 0, ctypes.byref(code))
+    return code.value

@@ -1,0 +1,436 @@
+// capi.cu - extern "C" entry points of libforgert_b200.so.
+//
+// Argument checks, per-device state (SM count, error word, workspace), the
+// split planner and the kernel launches.  Declarations and contracts live in
+// include/forgert_attn.h; each entry point there names the reference launcher
+// it replaces.
+#include "decode_kernels.cuh"
+#include "rope_kernels.cuh"
+#include "../../include/forgert_attn.h"
+
+#include <cuda_runtime.h>
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+namespace {
+
+using fr::DecodeParams;
+
+constexpr int kVersion = 100;     // 0.1.0
+constexpr int kTile = 64;         // KV positions per pipeline stage
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = 32 * (kConsumerWarps + 1);
+
+thread_local int t_last_cuda = 0;
+std::atomic<unsigned long long> g_launches{0};   // kernels launched (or captured) by this library
+
+int cuda_fail(cudaError_t e) {
+    t_last_cuda = static_cast<int>(e);
+    return FR_ERR_CUDA;
+}
+
+struct DeviceState {
+    int sm_count = 0;
+    int* err = nullptr;          // device error word
+    void* ws = nullptr;          // split partial states
+    size_t ws_bytes = 0;
+    uint32_t attr_done = 0;      // bit per kernel instantiation: smem attribute set
+    int occupancy[8] = {0};      // CTAs/SM per instantiation (0 = not queried)
+};
+
+std::mutex g_mu;
+std::unordered_map<int, DeviceState> g_dev;
+
+// Returns the current device's state, creating it (cudaMalloc of the error
+// word) on first use.  First use must therefore happen outside graph capture.
+int get_state(DeviceState** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState& st = g_dev[dev];
+    if (!st.err) {
+        e = cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_fail(e);
+        e = cudaMalloc(&st.err, sizeof(int));
+        if (e != cudaSuccess) { st.err = nullptr; return cuda_fail(e); }
+        e = cudaMemset(st.err, 0, sizeof(int));
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
+    *out = &st;
+    return FR_OK;
+}
+
+bool is_capturing(cudaStream_t s) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) return false;
+    return cs != cudaStreamCaptureStatusNone;
+}
+
+int ensure_workspace(DeviceState* st, size_t bytes, cudaStream_t s) {
+    if (bytes <= st->ws_bytes) return FR_OK;
+    if (is_capturing(s)) return FR_ERR_WORKSPACE;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (bytes <= st->ws_bytes) return FR_OK;
+    if (st->ws) {
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(e);
+        cudaFree(st->ws);
+        st->ws = nullptr;
+        st->ws_bytes = 0;
+    }
+    const size_t grow = bytes + bytes / 4;
+    cudaError_t e = cudaMalloc(&st->ws, grow);
+    if (e != cudaSuccess) { st->ws = nullptr; return cuda_fail(e); }
+    st->ws_bytes = grow;
+    return FR_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// ------------------------------------------------------------- kernel table
+// One instantiation per (head_dim, head tile); the stage count keeps about
+// 100 KB of K/V in flight per CTA (two CTAs per SM).
+template <int D> struct Stages;
+template <> struct Stages<64> { static constexpr int value = 6; };
+template <> struct Stages<128> { static constexpr int value = 3; };
+
+template <int D, int NT>
+constexpr int kernel_slot() { return (D == 64 ? 0 : 2) + (NT - 1); }
+
+template <int D, int NT>
+int launch_split(DeviceState* st, const DecodeParams& p, dim3 grid, cudaStream_t s) {
+    constexpr int STG = Stages<D>::value;
+    using Smem = fr::SplitSmem<D, NT, kTile, STG, kConsumerWarps>;
+    auto kern = fr::split_decode_kernel<D, NT, kTile, STG, kConsumerWarps>;
+    constexpr int slot = kernel_slot<D, NT>();
+    if (!(st->attr_done & (1u << slot))) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(Smem::kBytes));
+        if (e != cudaSuccess) return cuda_fail(e);
+        st->attr_done |= (1u << slot);
+    }
+    kern<<<grid, kThreads, Smem::kBytes, s>>>(p);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    return FR_OK;
+}
+
+template <int D, int NT>
+int occupancy(DeviceState* st) {
+    constexpr int slot = kernel_slot<D, NT>();
+    if (st->occupancy[slot] == 0) {
+        constexpr int STG = Stages<D>::value;
+        using Smem = fr::SplitSmem<D, NT, kTile, STG, kConsumerWarps>;
+        auto kern = fr::split_decode_kernel<D, NT, kTile, STG, kConsumerWarps>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(Smem::kBytes));
+        int n = 0;
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, Smem::kBytes);
+        st->occupancy[slot] = (e == cudaSuccess && n > 0) ? n : 1;
+    }
+    return st->occupancy[slot];
+}
+
+struct Plan {
+    int nt = 1;            // 8-head tiles per CTA (1 or 2)
+    int head_groups = 1;   // CTAs per kv head along the query group
+    int num_splits = 1;
+    int split_len = 0;     // positions per split, multiple of kTile
+};
+
+// Splits the longest sequence so the grid fills the GPU about once:
+// units = batch * kv_heads * head_groups CTAs per split.
+Plan make_plan(int sm_count, int occ, int batch, int num_kv_heads, int group, int max_kv_len,
+               int min_waves) {
+    Plan pl;
+    pl.nt = group <= 8 ? 1 : 2;
+    pl.head_groups = (group + 8 * pl.nt - 1) / (8 * pl.nt);
+    const long long units = (long long)batch * num_kv_heads * pl.head_groups;
+    const int tiles = std::max(1, (max_kv_len + kTile - 1) / kTile);
+    const long long slots = (long long)sm_count * occ * min_waves;
+    long long want = std::max<long long>(1, slots / std::max<long long>(1, units));
+    want = std::min<long long>(want, tiles);
+    const int tps = (int)((tiles + want - 1) / want);
+    pl.split_len = tps * kTile;
+    pl.num_splits = (tiles + tps - 1) / tps;
+    return pl;
+}
+
+template <int D>
+int occupancy_for(DeviceState* st, int nt) {
+    return nt == 1 ? occupancy<D, 1>(st) : occupancy<D, 2>(st);
+}
+
+template <int D>
+int launch_for(DeviceState* st, int nt, const DecodeParams& p, dim3 grid, cudaStream_t s) {
+    return nt == 1 ? launch_split<D, 1>(st, p, grid, s) : launch_split<D, 2>(st, p, grid, s);
+}
+
+template <int D>
+int launch_merge(const float* ml, const float* acc, int num_states, long long row_stride,
+                 long long state_stride, int rows, __half* out, float* out_ml, float* out_acc,
+                 int mode, cudaStream_t s) {
+    fr::lse_merge_kernel<D><<<rows, D, 0, s>>>(ml, acc, num_states, row_stride, state_stride, out,
+                                               out_ml, out_acc, mode);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    return FR_OK;
+}
+
+size_t partial_bytes(long long rows, int splits, int head_dim) {
+    return (size_t)rows * splits * (2 + head_dim) * sizeof(float);
+}
+
+int check_heads(int num_heads, int num_kv_heads, int head_dim) {
+    if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return FR_ERR_INVALID_ARG;
+    if (head_dim != 64 && head_dim != 128) return FR_ERR_UNSUPPORTED;
+    return FR_OK;
+}
+
+// Shared driver of the decode-family entry points.
+//   final_out != nullptr : write fp16 output (merging splits if needed)
+//   state_ml  != nullptr : write one merged (m, l, acc) state per head row
+int run_decode(DecodeParams p, int batch, int max_kv_len, __half* final_out, float* state_ml,
+               float* state_acc, int min_waves, cudaStream_t s) {
+    DeviceState* st = nullptr;
+    int rc = get_state(&st);
+    if (rc != FR_OK) return rc;
+    const int D = p.row_stride / p.Hkv;
+    const int group = p.H / p.Hkv;
+    const int nt = group <= 8 ? 1 : 2;
+    const int occ = D == 64 ? occupancy_for<64>(st, nt) : occupancy_for<128>(st, nt);
+    Plan pl = make_plan(st->sm_count, occ, batch, p.Hkv, group, max_kv_len, min_waves);
+    p.G = group;
+    p.split_len = pl.split_len;
+    p.num_splits = pl.num_splits;
+    p.head_groups = pl.head_groups;
+    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
+    p.err = st->err;
+    const long long rows = (long long)batch * p.H;
+    const bool direct = final_out != nullptr && pl.num_splits == 1;
+    if (direct) {
+        p.write_final = 1;
+        p.out = final_out;
+    } else {
+        rc = ensure_workspace(st, partial_bytes(rows, pl.num_splits, D), s);
+        if (rc != FR_OK) return rc;
+        p.write_final = 0;
+        p.part_ml = static_cast<float*>(st->ws);
+        p.part_acc = p.part_ml + rows * pl.num_splits * 2;
+    }
+    dim3 grid(pl.num_splits, p.Hkv * pl.head_groups, batch);
+    rc = D == 64 ? launch_for<64>(st, pl.nt, p, grid, s) : launch_for<128>(st, pl.nt, p, grid, s);
+    if (rc != FR_OK || direct) return rc;
+    const int mode = final_out ? 0 : 1;
+    return D == 64 ? launch_merge<64>(p.part_ml, p.part_acc, pl.num_splits, pl.num_splits, 1,
+                                      (int)rows, final_out, state_ml, state_acc, mode, s)
+                   : launch_merge<128>(p.part_ml, p.part_acc, pl.num_splits, pl.num_splits, 1,
+                                       (int)rows, final_out, state_ml, state_acc, mode, s);
+}
+
+DecodeParams base_params(const void* q, int num_heads, int num_kv_heads, int head_dim) {
+    DecodeParams p{};
+    p.q = static_cast<const __half*>(q);
+    p.H = num_heads;
+    p.Hkv = num_kv_heads;
+    p.G = num_heads / num_kv_heads;
+    p.row_stride = (long long)num_kv_heads * head_dim;
+    return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fr_decode_attn(const void* q, const void* k_cache, const void* v_cache, void* out,
+                   int num_heads, int num_kv_heads, int head_dim, int kv_len, void* stream) {
+    if (!q || !k_cache || !v_cache || !out || kv_len <= 0) return FR_ERR_INVALID_ARG;
+    int rc = check_heads(num_heads, num_kv_heads, head_dim);
+    if (rc != FR_OK) return rc;
+    if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 4) || !aligned(out, 4))
+        return FR_ERR_MISALIGNED;
+    DecodeParams p = base_params(q, num_heads, num_kv_heads, head_dim);
+    p.k = static_cast<const __half*>(k_cache);
+    p.v = static_cast<const __half*>(v_cache);
+    p.kv_len = kv_len;
+    return run_decode(p, 1, kv_len, static_cast<__half*>(out), nullptr, nullptr, 1,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int fr_decode_attn_batched(const void* q, const void* const* k_caches,
+                           const void* const* v_caches, const int* kv_lens, void* out,
+                           int batch, int num_heads, int num_kv_heads, int head_dim,
+                           int max_kv_len, void* stream) {
+    if (!q || !k_caches || !v_caches || !kv_lens || !out || batch <= 0 || max_kv_len < 0)
+        return FR_ERR_INVALID_ARG;
+    int rc = check_heads(num_heads, num_kv_heads, head_dim);
+    if (rc != FR_OK) return rc;
+    if (!aligned(q, 4) || !aligned(out, 4) || !aligned(k_caches, 8) || !aligned(v_caches, 8) ||
+        !aligned(kv_lens, 4))
+        return FR_ERR_MISALIGNED;
+    DecodeParams p = base_params(q, num_heads, num_kv_heads, head_dim);
+    p.k_ptrs = reinterpret_cast<const __half* const*>(k_caches);
+    p.v_ptrs = reinterpret_cast<const __half* const*>(v_caches);
+    p.kv_lens = kv_lens;
+    // Ragged batches: several waves of shorter splits balance the tail.
+    return run_decode(p, batch, std::max(1, max_kv_len), static_cast<__half*>(out), nullptr,
+                      nullptr, 4, static_cast<cudaStream_t>(stream));
+}
+
+int fr_decode_attn_partial(const void* q, const void* k_cache, const void* v_cache, int kv_len,
+                           float* state_ml, float* state_acc, int num_heads, int num_kv_heads,
+                           int head_dim, void* stream) {
+    if (!q || !state_ml || !state_acc || kv_len < 0) return FR_ERR_INVALID_ARG;
+    if (kv_len > 0 && (!k_cache || !v_cache)) return FR_ERR_INVALID_ARG;
+    int rc = check_heads(num_heads, num_kv_heads, head_dim);
+    if (rc != FR_OK) return rc;
+    if ((kv_len > 0 && (!aligned(k_cache, 16) || !aligned(v_cache, 16))) || !aligned(q, 4) ||
+        !aligned(state_ml, 8) || !aligned(state_acc, 4))
+        return FR_ERR_MISALIGNED;
+    DecodeParams p = base_params(q, num_heads, num_kv_heads, head_dim);
+    p.k = static_cast<const __half*>(k_cache);
+    p.v = static_cast<const __half*>(v_cache);
+    p.kv_len = kv_len;
+    return run_decode(p, 1, std::max(1, kv_len), nullptr, state_ml, state_acc, 1,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int fr_lse_merge(const float* states_ml, const float* states_acc, int num_states, void* out,
+                 int num_heads, int head_dim, void* stream) {
+    if (!states_ml || !states_acc || !out || num_states <= 0 || num_heads <= 0)
+        return FR_ERR_INVALID_ARG;
+    if (head_dim != 64 && head_dim != 128) return FR_ERR_UNSUPPORTED;
+    if (!aligned(out, 2) || !aligned(states_ml, 8) || !aligned(states_acc, 4)) return FR_ERR_MISALIGNED;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    __half* o = static_cast<__half*>(out);
+    return head_dim == 64
+               ? launch_merge<64>(states_ml, states_acc, num_states, 1, num_heads, num_heads, o,
+                                  nullptr, nullptr, 0, s)
+               : launch_merge<128>(states_ml, states_acc, num_states, 1, num_heads, num_heads, o,
+                                   nullptr, nullptr, 0, s);
+}
+
+int fr_rope_tables(float* cos_tab, float* sin_tab, int max_seq_len, int head_dim, float base,
+                   float scale) {
+    if (!cos_tab || !sin_tab || max_seq_len <= 0 || head_dim <= 0 || (head_dim & 1) ||
+        !(base > 0.f) || !(scale > 0.f))
+        return FR_ERR_INVALID_ARG;
+    const int half_d = head_dim / 2;
+    std::vector<float> c((size_t)max_seq_len * half_d), s((size_t)max_seq_len * half_d);
+    for (int f = 0; f < half_d; ++f) {
+        const double inv = 1.0 / (std::pow((double)base, 2.0 * f / (double)head_dim) * (double)scale);
+        for (int pos = 0; pos < max_seq_len; ++pos) {
+            const double th = (double)pos * inv;
+            c[(size_t)pos * half_d + f] = (float)std::cos(th);
+            s[(size_t)pos * half_d + f] = (float)std::sin(th);
+        }
+    }
+    cudaError_t e = cudaMemcpy(cos_tab, c.data(), c.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e);
+    e = cudaMemcpy(sin_tab, s.data(), s.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return FR_OK;
+}
+
+int fr_rope_append(void* q, void* k, const void* v, void* k_cache, void* v_cache,
+                   const float* cos_tab, const float* sin_tab, int seq_len, int num_heads,
+                   int num_kv_heads, int head_dim, int pos_offset, void* stream) {
+    if (!q || !k || !v || !k_cache || !v_cache || !cos_tab || !sin_tab || seq_len <= 0 ||
+        pos_offset < 0)
+        return FR_ERR_INVALID_ARG;
+    int rc = check_heads(num_heads, num_kv_heads, head_dim);
+    if (rc != FR_OK) return rc;
+    if (!aligned(v, 16) || !aligned(v_cache, 16) || !aligned(q, 2) || !aligned(k, 2) ||
+        !aligned(k_cache, 2))
+        return FR_ERR_MISALIGNED;
+    fr::rope_append_kernel<<<seq_len, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<__half*>(q), static_cast<__half*>(k), static_cast<const __half*>(v),
+        static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), cos_tab, sin_tab,
+        num_heads, num_kv_heads, head_dim, pos_offset);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    return FR_OK;
+}
+
+int fr_prefill_attn(const void* q, const void* k, const void* v, void* out, int seq_len,
+                    int num_heads, int num_kv_heads, int head_dim, void* stream) {
+    if (!q || !k || !v || !out || seq_len <= 0) return FR_ERR_INVALID_ARG;
+    int rc = check_heads(num_heads, num_kv_heads, head_dim);
+    if (rc != FR_OK) return rc;
+    if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 4) || !aligned(out, 4))
+        return FR_ERR_MISALIGNED;
+    // Query position s is a "sequence" of length s + 1 over the shared cache.
+    DecodeParams p = base_params(q, num_heads, num_kv_heads, head_dim);
+    p.k = static_cast<const __half*>(k);
+    p.v = static_cast<const __half*>(v);
+    p.causal = 1;
+    p.causal_offset = 0;
+    return run_decode(p, seq_len, seq_len, static_cast<__half*>(out), nullptr, nullptr, 4,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int fr_reserve_workspace(size_t bytes) {
+    DeviceState* st = nullptr;
+    int rc = get_state(&st);
+    if (rc != FR_OK) return rc;
+    return ensure_workspace(st, bytes, nullptr);
+}
+
+size_t fr_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
+                                int max_kv_len) {
+    if (batch <= 0 || check_heads(num_heads, num_kv_heads, head_dim) != FR_OK) return 0;
+    DeviceState* st = nullptr;
+    if (get_state(&st) != FR_OK) return 0;
+    const int group = num_heads / num_kv_heads;
+    const int nt = group <= 8 ? 1 : 2;
+    const int occ = head_dim == 64 ? occupancy_for<64>(st, nt) : occupancy_for<128>(st, nt);
+    const int waves = batch > 1 ? 4 : 1;
+    Plan pl = make_plan(st->sm_count, occ, batch, num_kv_heads, group, std::max(1, max_kv_len), waves);
+    return partial_bytes((long long)batch * num_heads, pl.num_splits, head_dim);
+}
+
+int fr_get_device_error(int clear, int* device_code) {
+    DeviceState* st = nullptr;
+    int rc = get_state(&st);
+    if (rc != FR_OK) return rc;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e);
+    int code = 0;
+    e = cudaMemcpy(&code, st->err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (clear && code) {
+        e = cudaMemset(st->err, 0, sizeof(int));
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
+    if (device_code) *device_code = code;
+    return code ? FR_ERR_TIMEOUT : FR_OK;
+}
+
+int fr_last_cuda_error(void) { return t_last_cuda; }
+
+const char* fr_status_string(int status) {
+    switch (status) {
+        case FR_OK: return "ok";
+        case FR_ERR_INVALID_ARG: return "invalid argument";
+        case FR_ERR_UNSUPPORTED: return "unsupported head_dim (64 or 128)";
+        case FR_ERR_MISALIGNED: return "misaligned pointer";
+        case FR_ERR_CUDA: return "CUDA runtime error";
+        case FR_ERR_TIMEOUT: return "in-kernel wait timed out";
+        case FR_ERR_WORKSPACE: return "workspace too small during stream capture";
+        default: return "unknown status";
+    }
+}
+
+int fr_version(void) { return kVersion; }
+
+unsigned long long fr_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+}  // extern "C"

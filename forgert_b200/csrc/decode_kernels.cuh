@@ -1,0 +1,475 @@
+// decode_kernels.cuh - split-KV flash-decode attention for sm_100a.
+//
+// Replaces the per-q-head SIMT kernel `decode_attn_kernel_v4<D,4>`
+// (kernels/attention_decode.cu:418-533 of the reference), which launches one
+// CTA per query head, re-reads each KV head G times and walks all of kv_len
+// in one CTA.
+//
+// Work decomposition: one CTA per (sequence b, kv head, head group, KV split).
+// The CTA serves the whole GQA query group of its kv head (up to 16 query
+// heads), so every K/V byte is read from HBM exactly once per call.
+//
+// Data movement: warp NW (the producer) streams K and V rows of a
+// TILE-position tile into shared memory with cp.async.bulk (TMA bulk copy,
+// no multicast), one copy per cache row, into a STAGES-deep ring guarded by
+// full/empty mbarriers.  Rows are written at a 16-byte padded pitch so the
+// ldmatrix reads below are bank-conflict free.
+//
+// Math: the four consumer warps take 16 positions each of every tile and use
+// the tensor cores with the query group as the N dimension:
+//     S^T[pos, head]  = K[pos, :] . Q^T[:, head]      (mma m16n8k16, M = pos)
+//     O^T[d, head]   += V^T[d, pos] . P^T[pos, head]  (mma m16n8k16, M = d)
+// Q (fp16, exact) stays in registers as the B operand for the whole call;
+// scores and the online softmax state (m, l) are fp32 in the base-2 domain
+// (scale * log2 e folded into one multiply).  Each probability enters the
+// P.V product as two fp16 halves (P = P_hi + P_lo), so the product keeps
+// about 22 bits of P and matches the reference's fp32 P.V to fp32 rounding;
+// accumulation is fp32.  P^T reaches the B-operand layout through
+// movmatrix.trans, without a shared-memory round trip.
+//
+// Output: with one split the CTA normalises and writes fp16 directly.  With
+// several, each CTA writes its (m, l, acc[D]) partial state and
+// `lse_merge_kernel` combines the splits (the flash-decoding log-sum-exp
+// merge).
+#pragma once
+#include "fr_ptx.cuh"
+#include <cuda_fp16.h>
+#include <cstdint>
+#include <cfloat>
+
+namespace fr {
+
+struct DecodeParams {
+    const __half* q;             // [B, H, D]
+    const __half* k;             // K layer view [*, Hkv, D] (single-sequence / causal mode)
+    const __half* v;
+    const __half* const* k_ptrs; // [B] per-sequence K bases (batched mode) or nullptr
+    const __half* const* v_ptrs; // [B] per-sequence V bases (batched mode) or nullptr
+    const int* kv_lens;          // [B] per-sequence lengths (batched mode) or nullptr
+    int kv_len;                  // length when kv_lens == nullptr (and not causal)
+    int causal;                  // 1: sequence b attends to positions [0, b + 1 + causal_offset)
+    int causal_offset;
+    int H, Hkv, G;               // query heads, kv heads, group size H / Hkv
+    long long row_stride;        // elements between consecutive positions (Hkv * D)
+    int split_len;               // positions per split (multiple of TILE)
+    int num_splits;              // gridDim.x
+    int head_groups;             // gridDim.y / Hkv
+    float scale_log2;            // log2(e) / sqrt(D)
+    int write_final;             // 1: single split, write normalised fp16 to out
+    __half* out;                 // [B, H, D]
+    float* part_ml;              // [B, H, num_splits, 2] : (m in log2 units, l)
+    float* part_acc;             // [B, H, num_splits, D] : unnormalised accumulators
+    int* err;                    // device error word
+};
+
+template <int D>
+struct TileCfg {
+    static constexpr int kPitch = D + 8;            // halves per smem row (16-byte pad)
+    static constexpr int kRowBytes = D * 2;
+};
+
+__device__ __forceinline__ void record_error(int* err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+// Named barrier over the consumer warps only (the producer may have exited).
+__device__ __forceinline__ void consumer_sync(int nthreads) {
+    asm volatile("bar.sync 1, %0;" :: "r"(nthreads) : "memory");
+}
+
+// Same barrier, returning the AND of `pred` over the participating threads.
+__device__ __forceinline__ int consumer_sync_and(int pred, int nthreads) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.s32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, %2, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r) : "r"(pred), "r"(nthreads) : "memory");
+    return r;
+}
+
+template <int D, int NT, int TILE, int STAGES, int NW>
+struct SplitSmem {
+    static constexpr int kPitch = TileCfg<D>::kPitch;
+    static constexpr int kStageHalves = TILE * kPitch;
+    // K ring, V ring, then barriers.
+    static constexpr size_t kRingBytes = size_t(2) * STAGES * kStageHalves * sizeof(__half);
+    static constexpr size_t kBarOffset = kRingBytes;
+    static constexpr size_t kBytes = kRingBytes + 2 * STAGES * sizeof(uint64_t);
+    // Cross-warp merge area (reuses the K ring once every tile is consumed).
+    static constexpr size_t kMergeBytes =
+        size_t(NW) * (NT * 8) * D * sizeof(float) + size_t(NW) * (NT * 8) * 2 * sizeof(float);
+    static_assert(kMergeBytes <= size_t(STAGES) * kStageHalves * sizeof(__half),
+                  "merge area must fit in the K ring");
+};
+
+// ---------------------------------------------------------------------------
+// Split-KV decode kernel.
+//   grid  = (num_splits, Hkv * head_groups, B)
+//   block = 32 * (NW + 1): NW consumer warps + 1 producer warp
+// ---------------------------------------------------------------------------
+template <int D, int NT, int TILE, int STAGES, int NW>
+__global__ void __launch_bounds__(32 * (NW + 1))
+split_decode_kernel(const DecodeParams p) {
+    static_assert(D % 16 == 0, "head_dim must be a multiple of 16");
+    static_assert(TILE == 16 * NW, "each consumer warp owns one 16-row m-tile per stage");
+    using S = SplitSmem<D, NT, TILE, STAGES, NW>;
+    constexpr int kPitch = S::kPitch;
+    constexpr int GP = NT * 8;          // padded heads per CTA
+    constexpr int KSTEPS = D / 16;      // k-steps of the QK product
+    constexpr int DTILES = D / 16;      // m-tiles of the PV product
+    constexpr bool kSplitP = true;      // hi/lo fp16 split of P (fp32-grade P.V)
+
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    __half* kring = reinterpret_cast<__half*>(smem_raw);
+    __half* vring = kring + STAGES * S::kStageHalves;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + S::kBarOffset);
+    uint64_t* empty = full + STAGES;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / p.head_groups;
+    const int hgrp = blockIdx.y % p.head_groups;
+    const int b = blockIdx.z;
+
+    // Heads served by this CTA: h0 .. h0 + gcount - 1.
+    const int h0 = kvh * p.G + hgrp * GP;
+    const int gcount = min(GP, p.G - hgrp * GP);
+
+    // Sequence geometry.
+    int seq_len;
+    const __half* kbase;
+    const __half* vbase;
+    if (p.causal) {
+        seq_len = b + 1 + p.causal_offset;
+        kbase = p.k;
+        vbase = p.v;
+    } else if (p.k_ptrs) {
+        seq_len = p.kv_lens ? p.kv_lens[b] : p.kv_len;
+        kbase = p.k_ptrs[b];
+        vbase = p.v_ptrs[b];
+    } else {
+        seq_len = p.kv_lens ? p.kv_lens[b] : p.kv_len;
+        kbase = p.k;
+        vbase = p.v;
+    }
+    kbase += (size_t)kvh * D;
+    vbase += (size_t)kvh * D;
+    const int pos_begin = split * p.split_len;
+    const int pos_end = min(seq_len, pos_begin + p.split_len);
+    const int ntiles = pos_end > pos_begin ? (pos_end - pos_begin + TILE - 1) / TILE : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NW);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // ------------------------------------------------------------ producer
+    if (warp == NW) {
+        const uint64_t policy = l2_policy_evict_first();
+        int issued = 0;
+        for (int i = 0; i < ntiles; ++i) {
+            const int s = i % STAGES;
+            if (i >= STAGES) {
+                if (!mbar_wait_bounded(&empty[s], ((i / STAGES) - 1) & 1)) {
+                    record_error(p.err, kDevTimeoutEmpty);
+                    break;
+                }
+            }
+            const int t0 = pos_begin + i * TILE;
+            const int rows = min(TILE, pos_end - t0);
+            __half* kdst = kring + s * S::kStageHalves;
+            __half* vdst = vring + s * S::kStageHalves;
+            if (rows < TILE) {
+                // Tail tile: zero the rows no copy will fill, so the P.V
+                // product multiplies exact zeros by finite values.
+                constexpr int kChunks = kPitch * 2 / 16;   // 16-byte chunks per row
+                for (int c = lane; c < (TILE - rows) * kChunks; c += 32) {
+                    const int r = rows + c / kChunks;
+                    const int off = (c % kChunks) * 8;
+                    *reinterpret_cast<uint4*>(kdst + r * kPitch + off) = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4*>(vdst + r * kPitch + off) = make_uint4(0, 0, 0, 0);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+            }
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], uint32_t(rows) * 2u * D * 2u);
+            __syncwarp();
+            for (int r = lane; r < rows; r += 32) {
+                const size_t g = (size_t)(t0 + r) * p.row_stride;
+                bulk_g2s_evict_first(kdst + r * kPitch, kbase + g, D * 2, &full[s], policy);
+                bulk_g2s_evict_first(vdst + r * kPitch, vbase + g, D * 2, &full[s], policy);
+            }
+            ++issued;
+        }
+        // Drain: wait until every copy this CTA issued has landed, so no
+        // bulk copy is still writing shared memory when the CTA retires.
+        if (lane == 0) {
+            for (int i = max(0, issued - STAGES); i < issued; ++i) {
+                if (!mbar_wait_bounded(&full[i % STAGES], (i / STAGES) & 1)) {
+                    record_error(p.err, kDevTimeoutFull);
+                    break;
+                }
+            }
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------ consumers
+    const int g = lane >> 2;     // fragment row group
+    const int t = lane & 3;      // fragment column pair
+
+    // Q^T as the B operand of S^T = K Q^T: b0 = Q[head][ks*16 + 2t .. +1], b1 = +8.
+    uint32_t qb[KSTEPS][NT][2];
+    {
+        const __half* qrow_base = p.q + ((size_t)b * p.H + h0) * D;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int hj = nt * 8 + g;
+            const bool valid = hj < gcount;
+            const __half* qrow = qrow_base + (size_t)hj * D;
+#pragma unroll
+            for (int ks = 0; ks < KSTEPS; ++ks) {
+                qb[ks][nt][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * t) : 0u;
+                qb[ks][nt][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * t) : 0u;
+            }
+        }
+    }
+
+    float o[DTILES][NT][4];
+#pragma unroll
+    for (int dm = 0; dm < DTILES; ++dm)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) o[dm][nt][c] = 0.f;
+    float m_run[NT][2], l_run[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        m_run[nt][0] = m_run[nt][1] = -INFINITY;
+        l_run[nt][0] = l_run[nt][1] = 0.f;
+    }
+
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    // ldmatrix row/column offsets (see the fragment maps in the file header).
+    const int k_row = (lane & 7) + ((lane >> 3) & 1) * 8;
+    const int k_col = (lane >> 4) * 8;
+    const int v_row = (lane & 7) + ((lane >> 4) & 1) * 8;
+    const int v_col = ((lane >> 3) & 1) * 8;
+
+    for (int i = 0; i < ntiles; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1)) {
+            record_error(p.err, kDevTimeoutFull);
+            ok = false;
+            break;
+        }
+        const int row0 = warp * 16;
+        const int tpos0 = pos_begin + i * TILE + row0;     // first position of this warp's m-tile
+        if (tpos0 < pos_end) {
+            const __half* kst = kring + s * S::kStageHalves + row0 * kPitch;
+            const __half* vst = vring + s * S::kStageHalves + row0 * kPitch;
+
+            // ---- S^T = K Q^T (16 positions x GP heads)
+            float sacc[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
+            const uint32_t kaddr = smem_u32(kst + k_row * kPitch + k_col);
+#pragma unroll
+            for (int ks = 0; ks < KSTEPS; ++ks) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(a0, a1, a2, a3, kaddr + ks * 32);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                    mma_16816(sacc[nt], a0, a1, a2, a3, qb[ks][nt][0], qb[ks][nt][1]);
+            }
+
+            // ---- mask rows past the end of the split
+            const bool row_lo_ok = tpos0 + g < pos_end;
+            const bool row_hi_ok = tpos0 + g + 8 < pos_end;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                if (!row_lo_ok) { sacc[nt][0] = -INFINITY; sacc[nt][1] = -INFINITY; }
+                if (!row_hi_ok) { sacc[nt][2] = -INFINITY; sacc[nt][3] = -INFINITY; }
+            }
+
+            // ---- online softmax per head column (base 2)
+            uint32_t pb[NT][2];
+            uint32_t pl[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                float alpha[2];
+                float pr[4];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    float mx = fmaxf(sacc[nt][j], sacc[nt][j + 2]);
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    const float m_new = fmaxf(m_run[nt][j], mx * sl2);
+                    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+                    alpha[j] = fast_exp2(m_run[nt][j] - m_use);
+                    m_run[nt][j] = m_new;
+                    pr[j] = fast_exp2(fmaf(sacc[nt][j], sl2, -m_use));
+                    pr[j + 2] = fast_exp2(fmaf(sacc[nt][j + 2], sl2, -m_use));
+                    l_run[nt][j] = fmaf(l_run[nt][j], alpha[j], pr[j] + pr[j + 2]);
+                }
+#pragma unroll
+                for (int dm = 0; dm < DTILES; ++dm) {
+                    o[dm][nt][0] *= alpha[0];
+                    o[dm][nt][1] *= alpha[1];
+                    o[dm][nt][2] *= alpha[0];
+                    o[dm][nt][3] *= alpha[1];
+                }
+                // P^T fragments: rows = positions, cols = heads -> B layout
+                // (k = pos, n = head).  P = P_hi + P_lo, both fp16, so the
+                // P.V product keeps ~22 bits of each probability.
+                const __half2 h01 = __floats2half2_rn(pr[0], pr[1]);
+                const __half2 h23 = __floats2half2_rn(pr[2], pr[3]);
+                pb[nt][0] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h01));
+                pb[nt][1] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h23));
+                if (kSplitP) {
+                    const float2 f01 = __half22float2(h01);
+                    const float2 f23 = __half22float2(h23);
+                    pl[nt][0] = movmatrix_trans(pack_half2(pr[0] - f01.x, pr[1] - f01.y));
+                    pl[nt][1] = movmatrix_trans(pack_half2(pr[2] - f23.x, pr[3] - f23.y));
+                }
+            }
+
+            // ---- O^T += V^T P^T
+            const uint32_t vaddr = smem_u32(vst + v_row * kPitch + v_col);
+#pragma unroll
+            for (int dm = 0; dm < DTILES; ++dm) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4_trans(a0, a1, a2, a3, vaddr + dm * 32);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    mma_16816(o[dm][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+                    if (kSplitP) mma_16816(o[dm][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // Row sums: each lane summed its own positions; fold the 8 row groups.
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            float l = l_run[nt][j];
+            l += __shfl_xor_sync(0xffffffffu, l, 4);
+            l += __shfl_xor_sync(0xffffffffu, l, 8);
+            l += __shfl_xor_sync(0xffffffffu, l, 16);
+            l_run[nt][j] = l;
+        }
+
+    // Every consumer must be past its last ldmatrix before the K ring is
+    // reused as the merge area.
+    const int ok_all = consumer_sync_and(ok ? 1 : 0, NW * 32);
+    if (!ok_all) return;
+
+    // ---- cross-warp merge through shared memory
+    float* macc = reinterpret_cast<float*>(smem_raw);            // [NW][GP][D]
+    float* mml = macc + NW * GP * D;                              // [NW][GP][2]
+#pragma unroll
+    for (int dm = 0; dm < DTILES; ++dm)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int d = dm * 16 + g + ((c >> 1) << 3);
+                const int hj = nt * 8 + 2 * t + (c & 1);
+                macc[(warp * GP + hj) * D + d] = o[dm][nt][c];
+            }
+    if (g == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int hj = nt * 8 + 2 * t + j;
+                mml[(warp * GP + hj) * 2 + 0] = m_run[nt][j];
+                mml[(warp * GP + hj) * 2 + 1] = l_run[nt][j];
+            }
+    }
+    consumer_sync(NW * 32);
+
+    const size_t head_base = (size_t)b * p.H + h0;
+    for (int idx = threadIdx.x; idx < gcount * D; idx += NW * 32) {
+        const int hj = idx / D;
+        const int d = idx % D;
+        float mstar = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) mstar = fmaxf(mstar, mml[(w * GP + hj) * 2]);
+        const float muse = (mstar == -INFINITY) ? 0.f : mstar;
+        float acc = 0.f, l = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float sc = fast_exp2(mml[(w * GP + hj) * 2] - muse);
+            acc = fmaf(macc[(w * GP + hj) * D + d], sc, acc);
+            l = fmaf(mml[(w * GP + hj) * 2 + 1], sc, l);
+        }
+        const size_t hrow = head_base + hj;
+        if (p.write_final) {
+            p.out[hrow * D + d] = __float2half_rn(l > 0.f ? acc / l : 0.f);
+        } else {
+            const size_t pidx = hrow * p.num_splits + split;
+            p.part_acc[pidx * D + d] = acc;
+            if (d == 0) {
+                p.part_ml[pidx * 2 + 0] = mstar;
+                p.part_ml[pidx * 2 + 1] = l;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Log-sum-exp merge of partial states.
+//   grid = rows (one CTA per output head row), block = D threads.
+//   State s of row r sits at index i = r*row_stride + s*state_stride:
+//   m = ml[2i] (log2 units), l = ml[2i+1], acc = acc[i*D + d].
+//   mode 0: out[r*D + d] = fp16( sum_s acc_s 2^(m_s-m*) / sum_s l_s 2^(m_s-m*) )
+//   mode 1: merged state (m*, l*, acc*) into out_ml / out_acc, so a rank can
+//           hand one state per head to the cross-GPU exchange.
+// A row whose states are all empty (l = 0) yields zeros.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(D)
+lse_merge_kernel(const float* __restrict__ ml, const float* __restrict__ acc, int num_states,
+                 long long row_stride, long long state_stride, __half* __restrict__ out,
+                 float* __restrict__ out_ml, float* __restrict__ out_acc, int mode) {
+    const int r = blockIdx.x;
+    const int d = threadIdx.x;
+    const size_t base = (size_t)r * row_stride;
+    float mstar = -INFINITY;
+    for (int s = 0; s < num_states; ++s) mstar = fmaxf(mstar, ml[2 * (base + (size_t)s * state_stride)]);
+    const float muse = (mstar == -INFINITY) ? 0.f : mstar;
+    float a = 0.f, l = 0.f;
+    for (int s = 0; s < num_states; ++s) {
+        const size_t i = base + (size_t)s * state_stride;
+        const float sc = fast_exp2(ml[2 * i] - muse);
+        a = fmaf(acc[i * D + d], sc, a);
+        l = fmaf(ml[2 * i + 1], sc, l);
+    }
+    if (mode == 0) {
+        out[(size_t)r * D + d] = __float2half_rn(l > 0.f ? a / l : 0.f);
+    } else {
+        out_acc[(size_t)r * D + d] = a;
+        if (d == 0) {
+            out_ml[2 * r] = mstar;
+            out_ml[2 * r + 1] = l;
+        }
+    }
+}
+
+}  // namespace fr

@@ -1,0 +1,139 @@
+/*
+ * forgert_attn.h - C ABI of the B200 (sm_100a) flash-decode attention engine.
+ *
+ * Drop-in replacement for the attention launchers of ForgeRT
+ * (kernels/attention.cuh).  Plain C types only: device pointers are `void*`
+ * to fp16 (IEEE binary16) data, `stream` is a `cudaStream_t` passed as
+ * `void*` (NULL = the legacy default stream, as in the reference), and every
+ * entry point returns an `int` status instead of the reference's `void`.
+ *
+ * Layouts follow the reference runtime:
+ *   q, out            [num_heads, head_dim]                      (one token)
+ *   k_cache, v_cache  [>= kv_len, num_kv_heads, head_dim]        (one layer's view
+ *                     of the cache [layers x 2 x max_seq_len x num_kv_heads x head_dim],
+ *                     runtime/kv_cache.cpp:29-37)
+ *   query head h reads kv head h / (num_heads / num_kv_heads).
+ *
+ * Pointers are caller-owned device memory.  k/v bases must be 16-byte aligned
+ * (rows are moved with TMA bulk copies); q/out 4-byte aligned.
+ *
+ * Workspace: calls that split the KV range keep per-split (m, l, acc) partial
+ * states in a library-owned per-device buffer that grows on demand with
+ * cudaMalloc.  Growth cannot happen inside CUDA-graph capture, so size it with
+ * fr_reserve_workspace() before capturing; a capture that would need more
+ * returns FR_ERR_WORKSPACE.  The buffer is shared by all calls on a device:
+ * calls on different streams of one device must not overlap in time.
+ */
+#ifndef FORGERT_ATTN_H
+#define FORGERT_ATTN_H
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define FR_API __attribute__((visibility("default")))
+#else
+#define FR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FR_OK 0
+#define FR_ERR_INVALID_ARG 1   /* null pointer, non-positive size, H % Hkv != 0 */
+#define FR_ERR_UNSUPPORTED 2   /* head_dim not in {64, 128} */
+#define FR_ERR_MISALIGNED 3    /* k/v not 16-byte aligned, q/out not 4-byte aligned */
+#define FR_ERR_CUDA 4          /* a CUDA runtime call failed: see fr_last_cuda_error() */
+#define FR_ERR_TIMEOUT 5       /* a bounded in-kernel wait ran out (fr_get_device_error) */
+#define FR_ERR_WORKSPACE 6     /* workspace too small while a stream is capturing */
+
+/* Single-token decode attention over kv_len cached positions.
+ * Replaces decode_attn_v4_flash (kernels/attention.cuh:65-71; definition
+ * kernels/attention_decode.cu:535-556).  Output: out[h] = softmax(q[h].K^T /
+ * sqrt(D)) . V in fp16, fp32 accumulation.  kv_len must be >= 1. */
+FR_API int fr_decode_attn(const void* q, const void* k_cache, const void* v_cache, void* out,
+                   int num_heads, int num_kv_heads, int head_dim, int kv_len, void* stream);
+
+/* Batched, ragged decode: sequence b has its own cache bases and length.
+ * No reference counterpart (the reference decodes one sequence per call,
+ * attention.cuh:30); it generalises decode_attn_v4_flash to a batch.
+ *   q, out         [batch, num_heads, head_dim]
+ *   k_caches[b], v_caches[b]  device arrays (length batch) of device pointers,
+ *                  each a [>= kv_lens[b], num_kv_heads, head_dim] view
+ *   kv_lens        device array (length batch); 0 is allowed and yields zeros
+ *   max_kv_len     host upper bound of kv_lens (sizes the launch) */
+FR_API int fr_decode_attn_batched(const void* q, const void* const* k_caches,
+                           const void* const* v_caches, const int* kv_lens, void* out,
+                           int batch, int num_heads, int num_kv_heads, int head_dim,
+                           int max_kv_len, void* stream);
+
+/* Partial attention over positions [0, kv_len) of the given cache view:
+ * writes one log-sum-exp state per query head instead of an output, for
+ * KV ranges that are split across GPUs.  No reference counterpart.
+ *   state_ml  [num_heads, 2] fp32: (m, l), m = running max of score*log2(e)/sqrt(D)
+ *   state_acc [num_heads, head_dim] fp32: sum_t 2^(s_t - m) v_t
+ * kv_len == 0 yields the empty state (m = -inf, l = 0, acc = 0). */
+FR_API int fr_decode_attn_partial(const void* q, const void* k_cache, const void* v_cache,
+                           int kv_len, float* state_ml, float* state_acc, int num_heads,
+                           int num_kv_heads, int head_dim, void* stream);
+
+/* Log-sum-exp merge of num_states partial states per head (as written by
+ * fr_decode_attn_partial, stacked state-major: state s of head h at
+ * states_ml[(s*num_heads + h)*2] and states_acc[(s*num_heads + h)*head_dim]).
+ * out[h] = fp16( sum_s acc_s 2^(m_s - m*) / sum_s l_s 2^(m_s - m*) ).
+ * No reference counterpart (the reference never splits the KV range). */
+FR_API int fr_lse_merge(const float* states_ml, const float* states_acc, int num_states, void* out,
+                 int num_heads, int head_dim, void* stream);
+
+/* RoPE cos/sin tables [max_seq_len, head_dim/2] fp32 into caller-allocated
+ * device buffers: theta(pos, f) = pos / (base^(2f/head_dim) * scale), evaluated
+ * in fp64 on the host and rounded once.  Synchronous, like the reference.
+ * Replaces rope_precompute_tables (kernels/rope.cuh:227-231, rope.cu:28-56),
+ * minus its allocation. */
+FR_API int fr_rope_tables(float* cos_tab, float* sin_tab, int max_seq_len, int head_dim, float base,
+                   float scale);
+
+/* Fused decode prologue: NeoX (half-split) RoPE on q and k in place for
+ * tokens t < seq_len at position pos_offset + t, then appends the rotated k
+ * and v rows to the layer cache at row pos_offset + t.  Replaces the
+ * sequence rope_v2_fused (kernels/rope.cu:193-207) + the two KV-append
+ * cudaMemcpyAsync calls of runtime/executor.cpp:140-152.
+ *   q [seq_len, num_heads, head_dim], k, v [seq_len, num_kv_heads, head_dim] */
+FR_API int fr_rope_append(void* q, void* k, const void* v, void* k_cache, void* v_cache,
+                   const float* cos_tab, const float* sin_tab, int seq_len, int num_heads,
+                   int num_kv_heads, int head_dim, int pos_offset, void* stream);
+
+/* Causal prefill attention: query position s attends to positions 0..s.
+ * Replaces prefill_attn_causal (kernels/attention.cuh:76-82; definition
+ * kernels/attention_decode.cu:563-619).
+ *   q, out [seq_len, num_heads, head_dim]; k, v [seq_len, num_kv_heads, head_dim] */
+FR_API int fr_prefill_attn(const void* q, const void* k, const void* v, void* out, int seq_len,
+                    int num_heads, int num_kv_heads, int head_dim, void* stream);
+
+/* Grows the current device's workspace to at least `bytes` (call before
+ * CUDA-graph capture).  fr_decode_workspace_size() gives the bytes one call
+ * of fr_decode_attn_batched with these sizes needs (fr_decode_attn: batch 1). */
+FR_API int fr_reserve_workspace(size_t bytes);
+FR_API size_t fr_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
+                                int max_kv_len);
+
+/* Reads (and optionally clears) the current device's in-kernel error word:
+ * 0 = none, otherwise a bounded wait ran out (FR_ERR_TIMEOUT is returned by
+ * the status).  Synchronises the device. */
+FR_API int fr_get_device_error(int clear, int* device_code);
+
+/* Last CUDA error code (cudaError_t as int) seen by this thread's calls. */
+FR_API int fr_last_cuda_error(void);
+FR_API const char* fr_status_string(int status);
+FR_API int fr_version(void);
+
+/* Number of kernels this library has launched (or recorded into a CUDA graph
+ * under capture) in this process.  Diagnostics only; no reference
+ * counterpart. */
+FR_API unsigned long long fr_launch_count(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* FORGERT_ATTN_H */
