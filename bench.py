@@ -106,28 +106,44 @@ class ClockSampler:
         0x100: "display_clock_setting",
     }
 
-    def __init__(self, index: int, period_s: float = 0.005):
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
         self.samples = []
         self.period = period_s
         self.stop_ev = threading.Event()
         self.ok = False
         try:
             import pynvml
+            import torch
             pynvml.nvmlInit()
             self.nvml = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.h = self._handle(pynvml, torch, cuda_index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
             self.ok = True
         except Exception:
             self.nvml = None
         self.t = threading.Thread(target=self._run, daemon=True)
+
+    @staticmethod
+    def _handle(pynvml, torch, cuda_index):
+        """NVML handle of the CUDA device (matched by PCI bus id when possible)."""
+        try:
+            p = torch.cuda.get_device_properties(cuda_index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+            ids = [v for v in vis.split(",") if v.strip().isdigit()]
+            idx = int(ids[cuda_index]) if cuda_index < len(ids) else cuda_index
+            return pynvml.nvmlDeviceGetHandleByIndex(idx)
 
     def _run(self):
         n = self.nvml
         while not self.stop_ev.is_set():
             try:
                 mhz = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
-                rs = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                rs = self.reasons_fn(self.h)
                 self.samples.append((mhz, rs))
             except Exception:
                 pass

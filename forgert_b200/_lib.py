@@ -25,9 +25,12 @@ _i = ctypes.c_int
 _fp = ctypes.POINTER(ctypes.c_float)
 SIGNATURES = {
     "fr_decode_attn": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
-    "fr_decode_attn_batched": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
+    "fr_decode_attn_batched": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i,
+                                    ctypes.c_longlong, _i, _vp]),
     "fr_decode_attn_partial": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp]),
     "fr_lse_merge": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp]),
+    "fr_lse_merge_strided": (_i, [_vp, _vp, _i, _vp, _i, _i, ctypes.c_longlong,
+                                  ctypes.c_longlong, _vp]),
     "fr_rope_tables": (_i, [_vp, _vp, _i, _i, ctypes.c_float, ctypes.c_float]),
     "fr_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "fr_prefill_attn": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),

@@ -76,14 +76,15 @@ def prefill_attn_causal(q, k, v, out, seq_len: int, num_heads: int, num_kv_heads
         _stream(stream)))
 
 
-def decode_attn_batched(q, k_caches, v_caches, kv_lens, out, batch: int, num_heads: int,
-                        num_kv_heads: int, head_dim: int, max_kv_len: int, stream=None) -> None:
-    """Ragged batch: k_caches/v_caches are device arrays of per-sequence cache
-    bases (int64 tensor or pointer), kv_lens a device int32 array."""
+def decode_attn_batched(q, k_pool, v_pool, row_offsets, kv_lens, out, batch: int,
+                        num_heads: int, num_kv_heads: int, head_dim: int, pool_rows: int,
+                        max_kv_len: int, stream=None) -> None:
+    """Ragged batch over a KV pool [pool_rows, Hkv, D]: sequence b's rows start
+    at row_offsets[b] (device int64) and it has kv_lens[b] (device int32) of them."""
     lib = load()
     check("fr_decode_attn_batched", lib.fr_decode_attn_batched(
-        _ptr(q), _ptr(k_caches), _ptr(v_caches), _ptr(kv_lens), _ptr(out), batch, num_heads,
-        num_kv_heads, head_dim, max_kv_len, _stream(stream)))
+        _ptr(q), _ptr(k_pool), _ptr(v_pool), _ptr(row_offsets), _ptr(kv_lens), _ptr(out), batch,
+        num_heads, num_kv_heads, head_dim, pool_rows, max_kv_len, _stream(stream)))
 
 
 def decode_attn_partial(q, k_cache, v_cache, kv_len: int, state_ml, state_acc, num_heads: int,

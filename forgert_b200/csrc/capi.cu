@@ -1,17 +1,21 @@
 // capi.cu - extern "C" entry points of libforgert_b200.so.
 //
-// Argument checks, per-device state (SM count, error word, workspace), the
-// split planner and the kernel launches.  Declarations and contracts live in
-// include/forgert_attn.h; each entry point there names the reference launcher
-// it replaces.
+// Argument checks, per-device state (SM count, error word, workspace), TMA
+// tensor-map encoding, the split planner and the kernel launches.
+// Declarations and contracts live in include/forgert_attn.h; each entry point
+// there names the reference launcher it replaces.
 #include "decode_kernels.cuh"
 #include "rope_kernels.cuh"
 #include "../../include/forgert_attn.h"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -92,9 +96,46 @@ int ensure_workspace(DeviceState* st, size_t bytes, cudaStream_t s) {
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+// ------------------------------------------------------------ tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// View of a cache [rows][Hkv][D] fp16 as a 4-D tensor [rows][Hkv][D/64][64]
+// (innermost first below), box = 64 dims x kTile rows of one kv head,
+// 128-byte swizzle.  Rows >= `rows` read as zeros.
+int encode_kv_map(CUtensorMap* map, const void* base, int head_dim, int num_kv_heads,
+                  long long rows) {
+    std::memset(map, 0, sizeof(*map));
+    if (rows <= 0) return FR_OK;                      // never read (empty range)
+    if (rows > (1LL << 31)) return FR_ERR_INVALID_ARG;
+    auto fn = encode_fn();
+    if (!fn) return cuda_fail(cudaErrorNotSupported);
+    const cuuint64_t dims[4] = {64, (cuuint64_t)(head_dim / 64), (cuuint64_t)num_kv_heads,
+                                (cuuint64_t)rows};
+    const cuuint64_t strides[3] = {128, (cuuint64_t)head_dim * 2,
+                                   (cuuint64_t)num_kv_heads * head_dim * 2};
+    const cuuint32_t box[4] = {64, 1, 1, (cuuint32_t)kTile};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cuda_fail(cudaErrorInvalidValue);
+    return FR_OK;
+}
+
 // ------------------------------------------------------------- kernel table
-// One instantiation per (head_dim, head tile); the stage count keeps about
-// 100 KB of K/V in flight per CTA (two CTAs per SM).
+// One instantiation per (head_dim, head tile).  The stage count keeps 48 KB
+// (D=64, 6 stages) / 96 KB (D=128, 3 stages) of K/V in flight per CTA.
 template <int D> struct Stages;
 template <> struct Stages<64> { static constexpr int value = 6; };
 template <> struct Stages<128> { static constexpr int value = 3; };
@@ -103,7 +144,7 @@ template <int D, int NT>
 constexpr int kernel_slot() { return (D == 64 ? 0 : 2) + (NT - 1); }
 
 template <int D, int NT>
-int launch_split(DeviceState* st, const DecodeParams& p, dim3 grid, cudaStream_t s) {
+int prepare_kernel(DeviceState* st) {
     constexpr int STG = Stages<D>::value;
     using Smem = fr::SplitSmem<D, NT, kTile, STG, kConsumerWarps>;
     auto kern = fr::split_decode_kernel<D, NT, kTile, STG, kConsumerWarps>;
@@ -112,29 +153,24 @@ int launch_split(DeviceState* st, const DecodeParams& p, dim3 grid, cudaStream_t
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(Smem::kBytes));
         if (e != cudaSuccess) return cuda_fail(e);
+        int n = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, Smem::kBytes);
+        st->occupancy[slot] = (e == cudaSuccess && n > 0) ? n : 1;
         st->attr_done |= (1u << slot);
     }
+    return FR_OK;
+}
+
+template <int D, int NT>
+int launch_split(const DecodeParams& p, dim3 grid, cudaStream_t s) {
+    constexpr int STG = Stages<D>::value;
+    using Smem = fr::SplitSmem<D, NT, kTile, STG, kConsumerWarps>;
+    auto kern = fr::split_decode_kernel<D, NT, kTile, STG, kConsumerWarps>;
     kern<<<grid, kThreads, Smem::kBytes, s>>>(p);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return FR_OK;
-}
-
-template <int D, int NT>
-int occupancy(DeviceState* st) {
-    constexpr int slot = kernel_slot<D, NT>();
-    if (st->occupancy[slot] == 0) {
-        constexpr int STG = Stages<D>::value;
-        using Smem = fr::SplitSmem<D, NT, kTile, STG, kConsumerWarps>;
-        auto kern = fr::split_decode_kernel<D, NT, kTile, STG, kConsumerWarps>;
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(Smem::kBytes));
-        int n = 0;
-        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, Smem::kBytes);
-        st->occupancy[slot] = (e == cudaSuccess && n > 0) ? n : 1;
-    }
-    return st->occupancy[slot];
 }
 
 struct Plan {
@@ -144,16 +180,16 @@ struct Plan {
     int split_len = 0;     // positions per split, multiple of kTile
 };
 
-// Splits the longest sequence so the grid fills the GPU about once:
+// Splits the longest sequence so the grid fills the GPU about `waves` times:
 // units = batch * kv_heads * head_groups CTAs per split.
 Plan make_plan(int sm_count, int occ, int batch, int num_kv_heads, int group, int max_kv_len,
-               int min_waves) {
+               int waves) {
     Plan pl;
     pl.nt = group <= 8 ? 1 : 2;
     pl.head_groups = (group + 8 * pl.nt - 1) / (8 * pl.nt);
     const long long units = (long long)batch * num_kv_heads * pl.head_groups;
     const int tiles = std::max(1, (max_kv_len + kTile - 1) / kTile);
-    const long long slots = (long long)sm_count * occ * min_waves;
+    const long long slots = (long long)sm_count * occ * waves;
     long long want = std::max<long long>(1, slots / std::max<long long>(1, units));
     want = std::min<long long>(want, tiles);
     const int tps = (int)((tiles + want - 1) / want);
@@ -163,21 +199,10 @@ Plan make_plan(int sm_count, int occ, int batch, int num_kv_heads, int group, in
 }
 
 template <int D>
-int occupancy_for(DeviceState* st, int nt) {
-    return nt == 1 ? occupancy<D, 1>(st) : occupancy<D, 2>(st);
-}
-
-template <int D>
-int launch_for(DeviceState* st, int nt, const DecodeParams& p, dim3 grid, cudaStream_t s) {
-    return nt == 1 ? launch_split<D, 1>(st, p, grid, s) : launch_split<D, 2>(st, p, grid, s);
-}
-
-template <int D>
-int launch_merge(const float* ml, const float* acc, int num_states, long long row_stride,
-                 long long state_stride, int rows, __half* out, float* out_ml, float* out_acc,
-                 int mode, cudaStream_t s) {
-    fr::lse_merge_kernel<D><<<rows, D, 0, s>>>(ml, acc, num_states, row_stride, state_stride, out,
-                                               out_ml, out_acc, mode);
+int launch_merge(const float* ml, const float* acc, int num_states, fr::MergeStrides st, int rows,
+                 __half* out, float* out_ml, float* out_acc, int mode, cudaStream_t s) {
+    fr::lse_merge_kernel<D><<<rows, 32 * fr::kMergeWarps, 0, s>>>(ml, acc, num_states, st, out,
+                                                                  out_ml, out_acc, mode);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
@@ -194,19 +219,31 @@ int check_heads(int num_heads, int num_kv_heads, int head_dim) {
     return FR_OK;
 }
 
-// Shared driver of the decode-family entry points.
+int plan_for(DeviceState* st, int head_dim, int batch, int num_kv_heads, int group,
+             int max_kv_len, int waves, Plan* pl) {
+    const int nt = group <= 8 ? 1 : 2;
+    int rc = head_dim == 64 ? (nt == 1 ? prepare_kernel<64, 1>(st) : prepare_kernel<64, 2>(st))
+                            : (nt == 1 ? prepare_kernel<128, 1>(st) : prepare_kernel<128, 2>(st));
+    if (rc != FR_OK) return rc;
+    const int occ = st->occupancy[head_dim == 64 ? (nt - 1) : (2 + nt - 1)];
+    *pl = make_plan(st->sm_count, occ, batch, num_kv_heads, group, max_kv_len, waves);
+    return FR_OK;
+}
+
+// Shared driver of the decode-family entry points.  `p` carries the tensor
+// maps and the sequence geometry.
 //   final_out != nullptr : write fp16 output (merging splits if needed)
 //   state_ml  != nullptr : write one merged (m, l, acc) state per head row
-int run_decode(DecodeParams p, int batch, int max_kv_len, __half* final_out, float* state_ml,
-               float* state_acc, int min_waves, cudaStream_t s) {
+int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* final_out,
+               float* state_ml, float* state_acc, int waves, cudaStream_t s) {
     DeviceState* st = nullptr;
     int rc = get_state(&st);
     if (rc != FR_OK) return rc;
-    const int D = p.row_stride / p.Hkv;
+    const int D = head_dim;
     const int group = p.H / p.Hkv;
-    const int nt = group <= 8 ? 1 : 2;
-    const int occ = D == 64 ? occupancy_for<64>(st, nt) : occupancy_for<128>(st, nt);
-    Plan pl = make_plan(st->sm_count, occ, batch, p.Hkv, group, max_kv_len, min_waves);
+    Plan pl;
+    rc = plan_for(st, D, batch, p.Hkv, group, max_kv_len, waves, &pl);
+    if (rc != FR_OK) return rc;
     p.G = group;
     p.split_len = pl.split_len;
     p.num_splits = pl.num_splits;
@@ -226,23 +263,35 @@ int run_decode(DecodeParams p, int batch, int max_kv_len, __half* final_out, flo
         p.part_acc = p.part_ml + rows * pl.num_splits * 2;
     }
     dim3 grid(pl.num_splits, p.Hkv * pl.head_groups, batch);
-    rc = D == 64 ? launch_for<64>(st, pl.nt, p, grid, s) : launch_for<128>(st, pl.nt, p, grid, s);
+    if (D == 64)
+        rc = pl.nt == 1 ? launch_split<64, 1>(p, grid, s) : launch_split<64, 2>(p, grid, s);
+    else
+        rc = pl.nt == 1 ? launch_split<128, 1>(p, grid, s) : launch_split<128, 2>(p, grid, s);
     if (rc != FR_OK || direct) return rc;
     const int mode = final_out ? 0 : 1;
-    return D == 64 ? launch_merge<64>(p.part_ml, p.part_acc, pl.num_splits, pl.num_splits, 1,
-                                      (int)rows, final_out, state_ml, state_acc, mode, s)
-                   : launch_merge<128>(p.part_ml, p.part_acc, pl.num_splits, pl.num_splits, 1,
-                                       (int)rows, final_out, state_ml, state_acc, mode, s);
+    // split partials: state (r, s) at index r*num_splits + s
+    const fr::MergeStrides ms{2LL * pl.num_splits, 2, (long long)pl.num_splits * D, D};
+    return D == 64 ? launch_merge<64>(p.part_ml, p.part_acc, pl.num_splits, ms, (int)rows,
+                                      final_out, state_ml, state_acc, mode, s)
+                   : launch_merge<128>(p.part_ml, p.part_acc, pl.num_splits, ms, (int)rows,
+                                       final_out, state_ml, state_acc, mode, s);
 }
 
-DecodeParams base_params(const void* q, int num_heads, int num_kv_heads, int head_dim) {
-    DecodeParams p{};
+DecodeParams base_params(const void* q, int num_heads, int num_kv_heads) {
+    DecodeParams p;
+    std::memset(&p, 0, sizeof(p));
     p.q = static_cast<const __half*>(q);
     p.H = num_heads;
     p.Hkv = num_kv_heads;
     p.G = num_heads / num_kv_heads;
-    p.row_stride = (long long)num_kv_heads * head_dim;
     return p;
+}
+
+int encode_pair(DecodeParams* p, const void* k, const void* v, int head_dim, int num_kv_heads,
+                long long rows) {
+    int rc = encode_kv_map(&p->kmap, k, head_dim, num_kv_heads, rows);
+    if (rc != FR_OK) return rc;
+    return encode_kv_map(&p->vmap, v, head_dim, num_kv_heads, rows);
 }
 
 }  // namespace
@@ -256,32 +305,35 @@ int fr_decode_attn(const void* q, const void* k_cache, const void* v_cache, void
     if (rc != FR_OK) return rc;
     if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 4) || !aligned(out, 4))
         return FR_ERR_MISALIGNED;
-    DecodeParams p = base_params(q, num_heads, num_kv_heads, head_dim);
-    p.k = static_cast<const __half*>(k_cache);
-    p.v = static_cast<const __half*>(v_cache);
+    DecodeParams p = base_params(q, num_heads, num_kv_heads);
+    rc = encode_pair(&p, k_cache, v_cache, head_dim, num_kv_heads, kv_len);
+    if (rc != FR_OK) return rc;
     p.kv_len = kv_len;
-    return run_decode(p, 1, kv_len, static_cast<__half*>(out), nullptr, nullptr, 1,
+    return run_decode(p, head_dim, 1, kv_len, static_cast<__half*>(out), nullptr, nullptr, 1,
                       static_cast<cudaStream_t>(stream));
 }
 
-int fr_decode_attn_batched(const void* q, const void* const* k_caches,
-                           const void* const* v_caches, const int* kv_lens, void* out,
-                           int batch, int num_heads, int num_kv_heads, int head_dim,
+int fr_decode_attn_batched(const void* q, const void* k_pool, const void* v_pool,
+                           const long long* row_offsets, const int* kv_lens, void* out, int batch,
+                           int num_heads, int num_kv_heads, int head_dim, long long pool_rows,
                            int max_kv_len, void* stream) {
-    if (!q || !k_caches || !v_caches || !kv_lens || !out || batch <= 0 || max_kv_len < 0)
+    if (!q || !k_pool || !v_pool || !row_offsets || !kv_lens || !out || batch <= 0 ||
+        max_kv_len < 0 || pool_rows <= 0)
         return FR_ERR_INVALID_ARG;
     int rc = check_heads(num_heads, num_kv_heads, head_dim);
     if (rc != FR_OK) return rc;
-    if (!aligned(q, 4) || !aligned(out, 4) || !aligned(k_caches, 8) || !aligned(v_caches, 8) ||
-        !aligned(kv_lens, 4))
+    if (!aligned(q, 4) || !aligned(out, 4) || !aligned(k_pool, 16) || !aligned(v_pool, 16) ||
+        !aligned(row_offsets, 8) || !aligned(kv_lens, 4))
         return FR_ERR_MISALIGNED;
-    DecodeParams p = base_params(q, num_heads, num_kv_heads, head_dim);
-    p.k_ptrs = reinterpret_cast<const __half* const*>(k_caches);
-    p.v_ptrs = reinterpret_cast<const __half* const*>(v_caches);
+    DecodeParams p = base_params(q, num_heads, num_kv_heads);
+    rc = encode_pair(&p, k_pool, v_pool, head_dim, num_kv_heads, pool_rows);
+    if (rc != FR_OK) return rc;
+    p.row_offsets = row_offsets;
     p.kv_lens = kv_lens;
+    p.zero_tail = 1;
     // Ragged batches: several waves of shorter splits balance the tail.
-    return run_decode(p, batch, std::max(1, max_kv_len), static_cast<__half*>(out), nullptr,
-                      nullptr, 4, static_cast<cudaStream_t>(stream));
+    return run_decode(p, head_dim, batch, std::max(1, max_kv_len), static_cast<__half*>(out),
+                      nullptr, nullptr, 4, static_cast<cudaStream_t>(stream));
 }
 
 int fr_decode_attn_partial(const void* q, const void* k_cache, const void* v_cache, int kv_len,
@@ -294,27 +346,38 @@ int fr_decode_attn_partial(const void* q, const void* k_cache, const void* v_cac
     if ((kv_len > 0 && (!aligned(k_cache, 16) || !aligned(v_cache, 16))) || !aligned(q, 4) ||
         !aligned(state_ml, 8) || !aligned(state_acc, 4))
         return FR_ERR_MISALIGNED;
-    DecodeParams p = base_params(q, num_heads, num_kv_heads, head_dim);
-    p.k = static_cast<const __half*>(k_cache);
-    p.v = static_cast<const __half*>(v_cache);
+    DecodeParams p = base_params(q, num_heads, num_kv_heads);
+    rc = encode_pair(&p, k_cache, v_cache, head_dim, num_kv_heads, kv_len);
+    if (rc != FR_OK) return rc;
     p.kv_len = kv_len;
-    return run_decode(p, 1, std::max(1, kv_len), nullptr, state_ml, state_acc, 1,
+    return run_decode(p, head_dim, 1, std::max(1, kv_len), nullptr, state_ml, state_acc, 1,
                       static_cast<cudaStream_t>(stream));
 }
 
 int fr_lse_merge(const float* states_ml, const float* states_acc, int num_states, void* out,
                  int num_heads, int head_dim, void* stream) {
-    if (!states_ml || !states_acc || !out || num_states <= 0 || num_heads <= 0)
+    return fr_lse_merge_strided(states_ml, states_acc, num_states, out, num_heads, head_dim,
+                                2LL * num_heads, (long long)num_heads * head_dim, stream);
+}
+
+int fr_lse_merge_strided(const float* states_ml, const float* states_acc, int num_states,
+                         void* out, int num_heads, int head_dim, long long ml_state_stride,
+                         long long acc_state_stride, void* stream) {
+    if (!states_ml || !states_acc || !out || num_states <= 0 || num_heads <= 0 ||
+        ml_state_stride < 0 || acc_state_stride < 0)
         return FR_ERR_INVALID_ARG;
     if (head_dim != 64 && head_dim != 128) return FR_ERR_UNSUPPORTED;
-    if (!aligned(out, 2) || !aligned(states_ml, 8) || !aligned(states_acc, 4)) return FR_ERR_MISALIGNED;
+    if (!aligned(out, 2) || !aligned(states_ml, 8) || !aligned(states_acc, 4) ||
+        (ml_state_stride & 1))
+        return FR_ERR_MISALIGNED;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     __half* o = static_cast<__half*>(out);
+    const fr::MergeStrides ms{2, ml_state_stride, head_dim, acc_state_stride};
     return head_dim == 64
-               ? launch_merge<64>(states_ml, states_acc, num_states, 1, num_heads, num_heads, o,
-                                  nullptr, nullptr, 0, s)
-               : launch_merge<128>(states_ml, states_acc, num_states, 1, num_heads, num_heads, o,
-                                   nullptr, nullptr, 0, s);
+               ? launch_merge<64>(states_ml, states_acc, num_states, ms, num_heads, o, nullptr,
+                                  nullptr, 0, s)
+               : launch_merge<128>(states_ml, states_acc, num_states, ms, num_heads, o, nullptr,
+                                   nullptr, 0, s);
 }
 
 int fr_rope_tables(float* cos_tab, float* sin_tab, int max_seq_len, int head_dim, float base,
@@ -368,13 +431,13 @@ int fr_prefill_attn(const void* q, const void* k, const void* v, void* out, int 
     if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 4) || !aligned(out, 4))
         return FR_ERR_MISALIGNED;
     // Query position s is a "sequence" of length s + 1 over the shared cache.
-    DecodeParams p = base_params(q, num_heads, num_kv_heads, head_dim);
-    p.k = static_cast<const __half*>(k);
-    p.v = static_cast<const __half*>(v);
+    DecodeParams p = base_params(q, num_heads, num_kv_heads);
+    rc = encode_pair(&p, k, v, head_dim, num_kv_heads, seq_len);
+    if (rc != FR_OK) return rc;
     p.causal = 1;
     p.causal_offset = 0;
-    return run_decode(p, seq_len, seq_len, static_cast<__half*>(out), nullptr, nullptr, 4,
-                      static_cast<cudaStream_t>(stream));
+    return run_decode(p, head_dim, seq_len, seq_len, static_cast<__half*>(out), nullptr, nullptr,
+                      4, static_cast<cudaStream_t>(stream));
 }
 
 int fr_reserve_workspace(size_t bytes) {
@@ -390,11 +453,14 @@ size_t fr_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int 
     DeviceState* st = nullptr;
     if (get_state(&st) != FR_OK) return 0;
     const int group = num_heads / num_kv_heads;
-    const int nt = group <= 8 ? 1 : 2;
-    const int occ = head_dim == 64 ? occupancy_for<64>(st, nt) : occupancy_for<128>(st, nt);
-    const int waves = batch > 1 ? 4 : 1;
-    Plan pl = make_plan(st->sm_count, occ, batch, num_kv_heads, group, std::max(1, max_kv_len), waves);
-    return partial_bytes((long long)batch * num_heads, pl.num_splits, head_dim);
+    Plan pl1, pl4;
+    if (plan_for(st, head_dim, batch, num_kv_heads, group, std::max(1, max_kv_len), 1, &pl1) !=
+            FR_OK ||
+        plan_for(st, head_dim, batch, num_kv_heads, group, std::max(1, max_kv_len), 4, &pl4) !=
+            FR_OK)
+        return 0;
+    const int splits = std::max(pl1.num_splits, pl4.num_splits);
+    return partial_bytes((long long)batch * num_heads, splits, head_dim);
 }
 
 int fr_get_device_error(int clear, int* device_code) {

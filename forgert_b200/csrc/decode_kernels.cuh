@@ -9,13 +9,16 @@
 // The CTA serves the whole GQA query group of its kv head (up to 16 query
 // heads), so every K/V byte is read from HBM exactly once per call.
 //
-// Data movement: warp NW (the producer) streams K and V rows of a
-// TILE-position tile into shared memory with cp.async.bulk (TMA bulk copy,
-// no multicast), one copy per cache row, into a STAGES-deep ring guarded by
-// full/empty mbarriers.  Rows are written at a 16-byte padded pitch so the
-// ldmatrix reads below are bank-conflict free.
+// Data movement: warp NW (the producer) streams K and V tiles of TILE
+// positions x 64 head dims into shared memory with 4-D TMA tensor copies
+// (cp.async.bulk.tensor, no multicast): the tensor map views a cache as
+// [rows][kv_heads][D/64][64] fp16, one box = 64 dims x TILE rows of one kv
+// head, written with the 128-byte swizzle (16-byte chunk c of row r lands at
+// chunk c ^ (r & 7)), which makes the ldmatrix reads below conflict-free.
+// Tiles cycle through a STAGES-deep ring guarded by full/empty mbarriers.
+// Rows past the end of the cache come back from TMA as zeros.
 //
-// Math: the four consumer warps take 16 positions each of every tile and use
+// Math: the NW consumer warps take 16 positions each of every tile and use
 // the tensor cores with the query group as the N dimension:
 //     S^T[pos, head]  = K[pos, :] . Q^T[:, head]      (mma m16n8k16, M = pos)
 //     O^T[d, head]   += V^T[d, pos] . P^T[pos, head]  (mma m16n8k16, M = d)
@@ -33,6 +36,7 @@
 // merge).
 #pragma once
 #include "fr_ptx.cuh"
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cstdint>
 #include <cfloat>
@@ -40,17 +44,16 @@
 namespace fr {
 
 struct DecodeParams {
+    CUtensorMap kmap;            // K view [rows][Hkv][D/64][64] (see file header)
+    CUtensorMap vmap;            // V view, same geometry
     const __half* q;             // [B, H, D]
-    const __half* k;             // K layer view [*, Hkv, D] (single-sequence / causal mode)
-    const __half* v;
-    const __half* const* k_ptrs; // [B] per-sequence K bases (batched mode) or nullptr
-    const __half* const* v_ptrs; // [B] per-sequence V bases (batched mode) or nullptr
-    const int* kv_lens;          // [B] per-sequence lengths (batched mode) or nullptr
-    int kv_len;                  // length when kv_lens == nullptr (and not causal)
+    const long long* row_offsets;// [B] first tensor-map row of each sequence, or nullptr (0)
+    const int* kv_lens;          // [B] per-sequence lengths, or nullptr (use kv_len)
+    int kv_len;
     int causal;                  // 1: sequence b attends to positions [0, b + 1 + causal_offset)
     int causal_offset;
+    int zero_tail;               // 1: rows past a sequence's end may hold non-finite data
     int H, Hkv, G;               // query heads, kv heads, group size H / Hkv
-    long long row_stride;        // elements between consecutive positions (Hkv * D)
     int split_len;               // positions per split (multiple of TILE)
     int num_splits;              // gridDim.x
     int head_groups;             // gridDim.y / Hkv
@@ -60,12 +63,6 @@ struct DecodeParams {
     float* part_ml;              // [B, H, num_splits, 2] : (m in log2 units, l)
     float* part_acc;             // [B, H, num_splits, D] : unnormalised accumulators
     int* err;                    // device error word
-};
-
-template <int D>
-struct TileCfg {
-    static constexpr int kPitch = D + 8;            // halves per smem row (16-byte pad)
-    static constexpr int kRowBytes = D * 2;
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {
@@ -91,18 +88,28 @@ __device__ __forceinline__ int consumer_sync_and(int pred, int nthreads) {
 
 template <int D, int NT, int TILE, int STAGES, int NW>
 struct SplitSmem {
-    static constexpr int kPitch = TileCfg<D>::kPitch;
-    static constexpr int kStageHalves = TILE * kPitch;
-    // K ring, V ring, then barriers.
-    static constexpr size_t kRingBytes = size_t(2) * STAGES * kStageHalves * sizeof(__half);
+    static constexpr int kSub = D / 64;                            // 128-byte column blocks
+    static constexpr int kSubBytes = TILE * 128;                   // one [TILE][64] box
+    static constexpr int kTileBytes = kSub * kSubBytes;            // K (or V) of one stage
+    static constexpr size_t kRingBytes = size_t(2) * STAGES * kTileBytes;
     static constexpr size_t kBarOffset = kRingBytes;
-    static constexpr size_t kBytes = kRingBytes + 2 * STAGES * sizeof(uint64_t);
-    // Cross-warp merge area (reuses the K ring once every tile is consumed).
+    // +1024: the ring is realigned to 1024 bytes (128-byte swizzle atom).
+    static constexpr size_t kBytes = 1024 + kRingBytes + 2 * STAGES * sizeof(uint64_t);
+    // Cross-warp merge area (reuses the ring once every tile is consumed).
     static constexpr size_t kMergeBytes =
         size_t(NW) * (NT * 8) * D * sizeof(float) + size_t(NW) * (NT * 8) * 2 * sizeof(float);
-    static_assert(kMergeBytes <= size_t(STAGES) * kStageHalves * sizeof(__half),
-                  "merge area must fit in the K ring");
+    static_assert(kMergeBytes <= kRingBytes, "merge area must fit in the ring");
+    static_assert(kSubBytes % 1024 == 0, "swizzled boxes must stay 1024-byte aligned");
 };
+
+// Byte offset of the 16-byte chunk holding element (row r, column col) of a
+// [rows][D] tile stored as D/64 swizzled [rows][64] boxes.
+template <int TILE>
+__device__ __forceinline__ uint32_t swz_offset(int r, int col) {
+    const int sub = col >> 6;
+    const int chunk = (col & 63) >> 3;
+    return uint32_t(sub * TILE * 128 + r * 128 + ((chunk ^ (r & 7)) << 4));
+}
 
 // ---------------------------------------------------------------------------
 // Split-KV decode kernel.
@@ -111,20 +118,20 @@ struct SplitSmem {
 // ---------------------------------------------------------------------------
 template <int D, int NT, int TILE, int STAGES, int NW>
 __global__ void __launch_bounds__(32 * (NW + 1))
-split_decode_kernel(const DecodeParams p) {
-    static_assert(D % 16 == 0, "head_dim must be a multiple of 16");
+split_decode_kernel(const __grid_constant__ DecodeParams p) {
+    static_assert(D % 64 == 0, "head_dim must be a multiple of 64");
     static_assert(TILE == 16 * NW, "each consumer warp owns one 16-row m-tile per stage");
     using S = SplitSmem<D, NT, TILE, STAGES, NW>;
-    constexpr int kPitch = S::kPitch;
     constexpr int GP = NT * 8;          // padded heads per CTA
     constexpr int KSTEPS = D / 16;      // k-steps of the QK product
     constexpr int DTILES = D / 16;      // m-tiles of the PV product
     constexpr bool kSplitP = true;      // hi/lo fp16 split of P (fp32-grade P.V)
 
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    __half* kring = reinterpret_cast<__half*>(smem_raw);
-    __half* vring = kring + STAGES * S::kStageHalves;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + S::kBarOffset);
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    unsigned char* kring = smem;
+    unsigned char* vring = smem + STAGES * S::kTileBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
     uint64_t* empty = full + STAGES;
 
     const int warp = threadIdx.x >> 5;
@@ -139,24 +146,8 @@ split_decode_kernel(const DecodeParams p) {
     const int gcount = min(GP, p.G - hgrp * GP);
 
     // Sequence geometry.
-    int seq_len;
-    const __half* kbase;
-    const __half* vbase;
-    if (p.causal) {
-        seq_len = b + 1 + p.causal_offset;
-        kbase = p.k;
-        vbase = p.v;
-    } else if (p.k_ptrs) {
-        seq_len = p.kv_lens ? p.kv_lens[b] : p.kv_len;
-        kbase = p.k_ptrs[b];
-        vbase = p.v_ptrs[b];
-    } else {
-        seq_len = p.kv_lens ? p.kv_lens[b] : p.kv_len;
-        kbase = p.k;
-        vbase = p.v;
-    }
-    kbase += (size_t)kvh * D;
-    vbase += (size_t)kvh * D;
+    const int seq_len = p.causal ? b + 1 + p.causal_offset : (p.kv_lens ? p.kv_lens[b] : p.kv_len);
+    const long long row_base = p.row_offsets ? p.row_offsets[b] : 0;
     const int pos_begin = split * p.split_len;
     const int pos_end = min(seq_len, pos_begin + p.split_len);
     const int ntiles = pos_end > pos_begin ? (pos_end - pos_begin + TILE - 1) / TILE : 0;
@@ -172,45 +163,32 @@ split_decode_kernel(const DecodeParams p) {
 
     // ------------------------------------------------------------ producer
     if (warp == NW) {
-        const uint64_t policy = l2_policy_evict_first();
         int issued = 0;
-        for (int i = 0; i < ntiles; ++i) {
-            const int s = i % STAGES;
-            if (i >= STAGES) {
-                if (!mbar_wait_bounded(&empty[s], ((i / STAGES) - 1) & 1)) {
-                    record_error(p.err, kDevTimeoutEmpty);
-                    break;
+        if (lane == 0 && ntiles > 0) {
+            prefetch_tensormap(&p.kmap);
+            prefetch_tensormap(&p.vmap);
+            const uint64_t policy = l2_policy_evict_first();
+            for (int i = 0; i < ntiles; ++i) {
+                const int s = i % STAGES;
+                if (i >= STAGES) {
+                    if (!mbar_wait_bounded(&empty[s], ((i / STAGES) - 1) & 1)) {
+                        record_error(p.err, kDevTimeoutEmpty);
+                        break;
+                    }
                 }
-            }
-            const int t0 = pos_begin + i * TILE;
-            const int rows = min(TILE, pos_end - t0);
-            __half* kdst = kring + s * S::kStageHalves;
-            __half* vdst = vring + s * S::kStageHalves;
-            if (rows < TILE) {
-                // Tail tile: zero the rows no copy will fill, so the P.V
-                // product multiplies exact zeros by finite values.
-                constexpr int kChunks = kPitch * 2 / 16;   // 16-byte chunks per row
-                for (int c = lane; c < (TILE - rows) * kChunks; c += 32) {
-                    const int r = rows + c / kChunks;
-                    const int off = (c % kChunks) * 8;
-                    *reinterpret_cast<uint4*>(kdst + r * kPitch + off) = make_uint4(0, 0, 0, 0);
-                    *reinterpret_cast<uint4*>(vdst + r * kPitch + off) = make_uint4(0, 0, 0, 0);
+                const int row = int(row_base + pos_begin + i * TILE);
+                mbar_arrive_expect_tx(&full[s], uint32_t(2 * S::kTileBytes));
+#pragma unroll
+                for (int sub = 0; sub < S::kSub; ++sub) {
+                    tma_load_4d(kring + s * S::kTileBytes + sub * S::kSubBytes, &p.kmap, 0, sub,
+                                kvh, row, &full[s], policy);
+                    tma_load_4d(vring + s * S::kTileBytes + sub * S::kSubBytes, &p.vmap, 0, sub,
+                                kvh, row, &full[s], policy);
                 }
-                fence_proxy_async_smem();
-                __syncwarp();
+                ++issued;
             }
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], uint32_t(rows) * 2u * D * 2u);
-            __syncwarp();
-            for (int r = lane; r < rows; r += 32) {
-                const size_t g = (size_t)(t0 + r) * p.row_stride;
-                bulk_g2s_evict_first(kdst + r * kPitch, kbase + g, D * 2, &full[s], policy);
-                bulk_g2s_evict_first(vdst + r * kPitch, vbase + g, D * 2, &full[s], policy);
-            }
-            ++issued;
-        }
-        // Drain: wait until every copy this CTA issued has landed, so no
-        // bulk copy is still writing shared memory when the CTA retires.
-        if (lane == 0) {
+            // Drain: wait until every copy this CTA issued has landed, so no
+            // TMA write is still in flight when the CTA retires.
             for (int i = max(0, issued - STAGES); i < issued; ++i) {
                 if (!mbar_wait_bounded(&full[i % STAGES], (i / STAGES) & 1)) {
                     record_error(p.err, kDevTimeoutFull);
@@ -258,11 +236,14 @@ split_decode_kernel(const DecodeParams p) {
 
     const float sl2 = p.scale_log2;
     bool ok = true;
-    // ldmatrix row/column offsets (see the fragment maps in the file header).
-    const int k_row = (lane & 7) + ((lane >> 3) & 1) * 8;
+    // ldmatrix rows/columns of this lane (see the fragment maps in the file header).
+    const int row0 = warp * 16;
+    const int k_row = row0 + (lane & 7) + ((lane >> 3) & 1) * 8;
     const int k_col = (lane >> 4) * 8;
-    const int v_row = (lane & 7) + ((lane >> 4) & 1) * 8;
+    const int v_row = row0 + (lane & 7) + ((lane >> 4) & 1) * 8;
     const int v_col = ((lane >> 3) & 1) * 8;
+    const uint32_t kring_s = smem_u32(kring);
+    const uint32_t vring_s = smem_u32(vring);
 
     for (int i = 0; i < ntiles; ++i) {
         const int s = i % STAGES;
@@ -271,11 +252,26 @@ split_decode_kernel(const DecodeParams p) {
             ok = false;
             break;
         }
-        const int row0 = warp * 16;
         const int tpos0 = pos_begin + i * TILE + row0;     // first position of this warp's m-tile
         if (tpos0 < pos_end) {
-            const __half* kst = kring + s * S::kStageHalves + row0 * kPitch;
-            const __half* vst = vring + s * S::kStageHalves + row0 * kPitch;
+            const uint32_t kst = kring_s + s * S::kTileBytes;
+            const uint32_t vst = vring_s + s * S::kTileBytes;
+            const int valid_rows = pos_end - tpos0;        // rows >= this are past the end
+            bool fenced = false;
+            if (p.zero_tail && valid_rows < 16) {
+                // Rows past the sequence may hold anything (other sequences'
+                // rows of a pool); zero this warp's V rows there so that
+                // P = 0 multiplies finite values.
+                unsigned char* vbase = vring + s * S::kTileBytes;
+                for (int c = lane; c < (16 - valid_rows) * S::kSub * 8; c += 32) {
+                    const int r = row0 + valid_rows + c / (S::kSub * 8);
+                    const int rest = c % (S::kSub * 8);
+                    *reinterpret_cast<uint4*>(vbase + (rest >> 3) * S::kSubBytes + r * 128 +
+                                              (rest & 7) * 16) = make_uint4(0, 0, 0, 0);
+                }
+                __syncwarp();
+                fenced = true;
+            }
 
             // ---- S^T = K Q^T (16 positions x GP heads)
             float sacc[NT][4];
@@ -283,19 +279,18 @@ split_decode_kernel(const DecodeParams p) {
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
-            const uint32_t kaddr = smem_u32(kst + k_row * kPitch + k_col);
 #pragma unroll
             for (int ks = 0; ks < KSTEPS; ++ks) {
                 uint32_t a0, a1, a2, a3;
-                ldsm_x4(a0, a1, a2, a3, kaddr + ks * 32);
+                ldsm_x4(a0, a1, a2, a3, kst + swz_offset<TILE>(k_row, ks * 16 + k_col));
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
                     mma_16816(sacc[nt], a0, a1, a2, a3, qb[ks][nt][0], qb[ks][nt][1]);
             }
 
             // ---- mask rows past the end of the split
-            const bool row_lo_ok = tpos0 + g < pos_end;
-            const bool row_hi_ok = tpos0 + g + 8 < pos_end;
+            const bool row_lo_ok = g < valid_rows;
+            const bool row_hi_ok = g + 8 < valid_rows;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 if (!row_lo_ok) { sacc[nt][0] = -INFINITY; sacc[nt][1] = -INFINITY; }
@@ -331,8 +326,7 @@ split_decode_kernel(const DecodeParams p) {
                     o[dm][nt][3] *= alpha[1];
                 }
                 // P^T fragments: rows = positions, cols = heads -> B layout
-                // (k = pos, n = head).  P = P_hi + P_lo, both fp16, so the
-                // P.V product keeps ~22 bits of each probability.
+                // (k = pos, n = head).  P = P_hi + P_lo, both fp16.
                 const __half2 h01 = __floats2half2_rn(pr[0], pr[1]);
                 const __half2 h23 = __floats2half2_rn(pr[2], pr[3]);
                 pb[nt][0] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h01));
@@ -346,17 +340,18 @@ split_decode_kernel(const DecodeParams p) {
             }
 
             // ---- O^T += V^T P^T
-            const uint32_t vaddr = smem_u32(vst + v_row * kPitch + v_col);
 #pragma unroll
             for (int dm = 0; dm < DTILES; ++dm) {
                 uint32_t a0, a1, a2, a3;
-                ldsm_x4_trans(a0, a1, a2, a3, vaddr + dm * 32);
+                ldsm_x4_trans(a0, a1, a2, a3, vst + swz_offset<TILE>(v_row, dm * 16 + v_col));
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     mma_16816(o[dm][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
                     if (kSplitP) mma_16816(o[dm][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
                 }
             }
+            // Generic-proxy writes into a stage the TMA will refill later.
+            if (fenced) fence_proxy_async_smem();
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -374,13 +369,13 @@ split_decode_kernel(const DecodeParams p) {
             l_run[nt][j] = l;
         }
 
-    // Every consumer must be past its last ldmatrix before the K ring is
+    // Every consumer must be past its last ldmatrix before the ring is
     // reused as the merge area.
     const int ok_all = consumer_sync_and(ok ? 1 : 0, NW * 32);
     if (!ok_all) return;
 
     // ---- cross-warp merge through shared memory
-    float* macc = reinterpret_cast<float*>(smem_raw);            // [NW][GP][D]
+    float* macc = reinterpret_cast<float*>(smem);                 // [NW][GP][D]
     float* mml = macc + NW * GP * D;                              // [NW][GP][2]
 #pragma unroll
     for (int dm = 0; dm < DTILES; ++dm)
@@ -435,39 +430,78 @@ split_decode_kernel(const DecodeParams p) {
 
 // ---------------------------------------------------------------------------
 // Log-sum-exp merge of partial states.
-//   grid = rows (one CTA per output head row), block = D threads.
-//   State s of row r sits at index i = r*row_stride + s*state_stride:
-//   m = ml[2i] (log2 units), l = ml[2i+1], acc = acc[i*D + d].
+//   grid = rows (one CTA per output head row), block = 256 threads (8 warps).
+//   State s of row r: (m, l) = ml[r*ml_rs + s*ml_ss + {0, 1}] (m in log2
+//   units), acc = acc[r*acc_rs + s*acc_ss + d]  (strides in floats).
+//   Warp w folds states w, w+8, ... with online rescaling; lane owns dims
+//   lane + 32j.  The warps' (m, l, acc) are folded once more in shared memory.
 //   mode 0: out[r*D + d] = fp16( sum_s acc_s 2^(m_s-m*) / sum_s l_s 2^(m_s-m*) )
-//   mode 1: merged state (m*, l*, acc*) into out_ml / out_acc, so a rank can
-//           hand one state per head to the cross-GPU exchange.
+//   mode 1: merged state (m*, l*, acc*) into out_ml[2r..] / out_acc[r*D..],
+//           so a rank can hand one state per head to the cross-GPU exchange.
 // A row whose states are all empty (l = 0) yields zeros.
 // ---------------------------------------------------------------------------
+struct MergeStrides {
+    long long ml_rs, ml_ss, acc_rs, acc_ss;
+};
+
+constexpr int kMergeWarps = 8;
+
 template <int D>
-__global__ void __launch_bounds__(D)
+__global__ void __launch_bounds__(32 * kMergeWarps)
 lse_merge_kernel(const float* __restrict__ ml, const float* __restrict__ acc, int num_states,
-                 long long row_stride, long long state_stride, __half* __restrict__ out,
-                 float* __restrict__ out_ml, float* __restrict__ out_acc, int mode) {
+                 const MergeStrides st, __half* __restrict__ out, float* __restrict__ out_ml,
+                 float* __restrict__ out_acc, int mode) {
+    constexpr int VEC = D / 32;
+    __shared__ float s_acc[kMergeWarps][D];
+    __shared__ float s_m[kMergeWarps], s_l[kMergeWarps];
     const int r = blockIdx.x;
-    const int d = threadIdx.x;
-    const size_t base = (size_t)r * row_stride;
-    float mstar = -INFINITY;
-    for (int s = 0; s < num_states; ++s) mstar = fmaxf(mstar, ml[2 * (base + (size_t)s * state_stride)]);
-    const float muse = (mstar == -INFINITY) ? 0.f : mstar;
-    float a = 0.f, l = 0.f;
-    for (int s = 0; s < num_states; ++s) {
-        const size_t i = base + (size_t)s * state_stride;
-        const float sc = fast_exp2(ml[2 * i] - muse);
-        a = fmaf(acc[i * D + d], sc, a);
-        l = fmaf(ml[2 * i + 1], sc, l);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const float* mlr = ml + (size_t)r * st.ml_rs;
+    const float* accr = acc + (size_t)r * st.acc_rs;
+
+    float m = -INFINITY, l = 0.f, a[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) a[j] = 0.f;
+    for (int s = warp; s < num_states; s += kMergeWarps) {
+        const float ms = mlr[(size_t)s * st.ml_ss];
+        const float ls = mlr[(size_t)s * st.ml_ss + 1];
+        float v[VEC];
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) v[j] = accr[(size_t)s * st.acc_ss + lane + 32 * j];
+        const float mn = fmaxf(m, ms);
+        const float mu = (mn == -INFINITY) ? 0.f : mn;
+        const float c_old = fast_exp2(m - mu), c_new = fast_exp2(ms - mu);
+        l = fmaf(l, c_old, ls * c_new);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) a[j] = fmaf(a[j], c_old, v[j] * c_new);
+        m = mn;
     }
-    if (mode == 0) {
-        out[(size_t)r * D + d] = __float2half_rn(l > 0.f ? a / l : 0.f);
-    } else {
-        out_acc[(size_t)r * D + d] = a;
-        if (d == 0) {
-            out_ml[2 * r] = mstar;
-            out_ml[2 * r + 1] = l;
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) s_acc[warp][lane + 32 * j] = a[j];
+    if (lane == 0) { s_m[warp] = m; s_l[warp] = l; }
+    __syncthreads();
+    if (threadIdx.x < D) {
+        const int d = threadIdx.x;
+        float mstar = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kMergeWarps; ++w) mstar = fmaxf(mstar, s_m[w]);
+        const float muse = (mstar == -INFINITY) ? 0.f : mstar;
+        float at = 0.f, lt = 0.f;
+#pragma unroll
+        for (int w = 0; w < kMergeWarps; ++w) {
+            const float sc = fast_exp2(s_m[w] - muse);
+            at = fmaf(s_acc[w][d], sc, at);
+            lt = fmaf(s_l[w], sc, lt);
+        }
+        if (mode == 0) {
+            out[(size_t)r * D + d] = __float2half_rn(lt > 0.f ? at / lt : 0.f);
+        } else {
+            out_acc[(size_t)r * D + d] = at;
+            if (d == 0) {
+                out_ml[2 * r] = mstar;
+                out_ml[2 * r + 1] = lt;
+            }
         }
     }
 }

@@ -81,6 +81,25 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
+// ------------------------------------------------ TMA tensor copy (no multicast)
+// 4-D tiled load described by a CUtensorMap that lives in kernel parameter
+// space (__grid_constant__).  Coordinates are element indices, innermost
+// first; out-of-bounds box elements are written as zeros and still count
+// towards the transaction bytes.
+__device__ __forceinline__ void tma_load_4d(void* dst_smem, const void* tmap, int c0, int c1,
+                                            int c2, int c3, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;"
+        :: "r"(smem_u32(dst_smem)), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+           "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
+}
+
 // ------------------------------------------------- TMA bulk copy (no multicast)
 // Copies `bytes` (multiple of 16, both addresses 16-byte aligned) from global
 // to this CTA's shared memory and signals completion on `bar` as tx bytes.

@@ -15,7 +15,7 @@
  *   query head h reads kv head h / (num_heads / num_kv_heads).
  *
  * Pointers are caller-owned device memory.  k/v bases must be 16-byte aligned
- * (rows are moved with TMA bulk copies); q/out 4-byte aligned.
+ * (tiles are moved with TMA tensor copies); q/out 4-byte aligned.
  *
  * Workspace: calls that split the KV range keep per-split (m, l, acc) partial
  * states in a library-owned per-device buffer that grows on demand with
@@ -54,18 +54,22 @@ extern "C" {
 FR_API int fr_decode_attn(const void* q, const void* k_cache, const void* v_cache, void* out,
                    int num_heads, int num_kv_heads, int head_dim, int kv_len, void* stream);
 
-/* Batched, ragged decode: sequence b has its own cache bases and length.
- * No reference counterpart (the reference decodes one sequence per call,
- * attention.cuh:30); it generalises decode_attn_v4_flash to a batch.
+/* Batched, ragged decode over a KV pool: sequence b's cache rows are pool
+ * rows [row_offsets[b], row_offsets[b] + kv_lens[b]) of
+ *   k_pool, v_pool  [pool_rows, num_kv_heads, head_dim] fp16 (16-byte aligned)
+ * (the reference's per-layer cache layout, with all sequences' rows in one
+ * allocation, as a paged/ragged serving cache keeps them).
  *   q, out         [batch, num_heads, head_dim]
- *   k_caches[b], v_caches[b]  device arrays (length batch) of device pointers,
- *                  each a [>= kv_lens[b], num_kv_heads, head_dim] view
- *   kv_lens        device array (length batch); 0 is allowed and yields zeros
- *   max_kv_len     host upper bound of kv_lens (sizes the launch) */
-FR_API int fr_decode_attn_batched(const void* q, const void* const* k_caches,
-                           const void* const* v_caches, const int* kv_lens, void* out,
-                           int batch, int num_heads, int num_kv_heads, int head_dim,
-                           int max_kv_len, void* stream);
+ *   row_offsets    device int64 array (length batch)
+ *   kv_lens        device int32 array (length batch); 0 is allowed and yields zeros
+ *   max_kv_len     host upper bound of kv_lens (sizes the launch)
+ * Rows of the pool past a sequence's end are never used, whatever they hold.
+ * No reference counterpart (the reference decodes one sequence per call,
+ * attention.cuh:30); it generalises decode_attn_v4_flash to a batch. */
+FR_API int fr_decode_attn_batched(const void* q, const void* k_pool, const void* v_pool,
+                                  const long long* row_offsets, const int* kv_lens, void* out,
+                                  int batch, int num_heads, int num_kv_heads, int head_dim,
+                                  long long pool_rows, int max_kv_len, void* stream);
 
 /* Partial attention over positions [0, kv_len) of the given cache view:
  * writes one log-sum-exp state per query head instead of an output, for
@@ -84,6 +88,16 @@ FR_API int fr_decode_attn_partial(const void* q, const void* k_cache, const void
  * No reference counterpart (the reference never splits the KV range). */
 FR_API int fr_lse_merge(const float* states_ml, const float* states_acc, int num_states, void* out,
                  int num_heads, int head_dim, void* stream);
+
+/* fr_lse_merge with explicit distances (in floats) between consecutive
+ * states of one head, for states gathered into one buffer per rank:
+ * state s of head h at states_ml[s*ml_state_stride + 2h] and
+ * states_acc[s*acc_state_stride + h*head_dim].  ml_state_stride must be even.
+ * No reference counterpart. */
+FR_API int fr_lse_merge_strided(const float* states_ml, const float* states_acc, int num_states,
+                                void* out, int num_heads, int head_dim,
+                                long long ml_state_stride, long long acc_state_stride,
+                                void* stream);
 
 /* RoPE cos/sin tables [max_seq_len, head_dim/2] fp32 into caller-allocated
  * device buffers: theta(pos, f) = pos / (base^(2f/head_dim) * scale), evaluated

@@ -117,25 +117,32 @@ def test_batched_ragged_small():
     lens = np.array([1, 64, 65, 300, 0, 2049, 17, 1500], np.int32)
     B = len(lens)
     q = W.normal_fp16(rng, (B, H, D))
-    ks = [W.normal_fp16(rng, (max(int(n), 1), Hkv, D)) for n in lens]
-    vs = [W.normal_fp16(rng, (max(int(n), 1), Hkv, D)) for n in lens]
-    out = run_batched(q, ks, vs, lens)
+    ks = [W.normal_fp16(rng, (int(n), Hkv, D)) for n in lens]
+    vs = [W.normal_fp16(rng, (int(n), Hkv, D)) for n in lens]
+    out = run_batched(q, ks, vs, lens, gap_rows=37)
     ref = O.batched_f64(q, ks, vs, lens)
     assert_close(out, ref, what="batched ragged")
     assert np.all(out[4] == 0), "kv_len 0 yields zeros"
 
 
-def run_batched(q, ks, vs, lens):
+def run_batched(q, ks, vs, lens, gap_rows=0):
+    """Packs the sequences into one KV pool, separated by `gap_rows` rows of
+    NaN (rows past a sequence's end must never reach the output)."""
     B, H, D = q.shape
-    Hkv = ks[0].shape[1]
-    kd = [dev(k) for k in ks]
-    vd = [dev(v) for v in vs]
-    kptr = torch.tensor([t.data_ptr() for t in kd], dtype=torch.int64, device="cuda")
-    vptr = torch.tensor([t.data_ptr() for t in vd], dtype=torch.int64, device="cuda")
+    Hkv = ks[0].shape[1] if ks else 1
+    offsets, parts_k, parts_v, row = [], [], [], 0
+    nan_rows = np.full((gap_rows, Hkv, D), np.nan, np.float16)
+    for k, v in zip(ks, vs):
+        offsets.append(row)
+        parts_k += [k, nan_rows]
+        parts_v += [v, nan_rows]
+        row += k.shape[0] + gap_rows
+    kd, vd = dev(np.concatenate(parts_k)), dev(np.concatenate(parts_v))
+    offs = dev(np.asarray(offsets, np.int64))
     lens_d = dev(np.asarray(lens, np.int32))
     qd = dev(q)
     out = nan_like(qd)
-    A.decode_attn_batched(qd, kptr, vptr, lens_d, out, B, H, Hkv, D, int(max(lens)))
+    A.decode_attn_batched(qd, kd, vd, offs, lens_d, out, B, H, Hkv, D, row, int(max(lens)))
     torch.cuda.synchronize()
     assert A.device_error() == 0
     return out.cpu().numpy()
