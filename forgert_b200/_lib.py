@@ -18,6 +18,7 @@ FR_ERR_MISALIGNED = 3
 FR_ERR_CUDA = 4
 FR_ERR_TIMEOUT = 5
 FR_ERR_WORKSPACE = 6
+FR_ERR_SCRATCH_LIMIT = 7
 
 # Every symbol include/forgert_attn.h declares, with its ctypes signature.
 _vp = ctypes.c_void_p
@@ -25,6 +26,7 @@ _i = ctypes.c_int
 _fp = ctypes.POINTER(ctypes.c_float)
 SIGNATURES = {
     "fr_decode_attn": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "fr_decode_attn_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "fr_decode_attn_batched": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i,
                                     ctypes.c_longlong, _i, _vp]),
     "fr_decode_attn_partial": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp]),

@@ -491,6 +491,9 @@ const char* fr_status_string(int status) {
         case FR_ERR_CUDA: return "CUDA runtime error";
         case FR_ERR_TIMEOUT: return "in-kernel wait timed out";
         case FR_ERR_WORKSPACE: return "workspace too small during stream capture";
+        case FR_ERR_SCRATCH_LIMIT:
+            return "problem needs more split scratch than the static no-alloc buffer holds "
+                   "(FR_NOALLOC_SCRATCH_BYTES)";
         default: return "unknown status";
     }
 }
@@ -500,3 +503,112 @@ int fr_version(void) { return kVersion; }
 unsigned long long fr_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode (fr_decode_attn_noalloc).
+//
+// Some callers cannot call cudaMalloc at all: code running inside another
+// framework's memory pool or allocator hooks, plugins loaded where the host
+// owns every device allocation, or a process that must not grow its device
+// footprint after start-up.  For them the split partial states live in this
+// file-scope device array instead of the grown-on-demand workspace.  Every
+// GPU that loads the library holds these FR_NOALLOC_SCRATCH_BYTES until the
+// process exits.
+//
+// Host code must not use the array's name as a device address (on the host
+// it is only a stand-in symbol): the set-up below asks the runtime for the
+// real address with cudaGetSymbolAddress, once per device, with that device
+// current, and passes that pointer to the kernels.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char fr_noalloc_scratch[FR_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+struct NoAllocDevice {
+    bool ready = false;
+    DeviceState st;              // sm_count / kernel attributes; err stays null
+    float* scratch = nullptr;    // device address of fr_noalloc_scratch on this device
+};
+
+std::mutex g_noalloc_mu;
+std::unordered_map<int, NoAllocDevice> g_noalloc;
+
+// First call on a device: symbol address, SM count, kernel attributes.  No
+// allocation anywhere (cudaGetSymbolAddress, cudaDeviceGetAttribute and
+// cudaFuncSetAttribute allocate nothing).
+int noalloc_setup(NoAllocDevice** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocDevice& nd = g_noalloc[dev];
+    if (!nd.ready) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, fr_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e);
+        e = cudaDeviceGetAttribute(&nd.st.sm_count, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_fail(e);
+        nd.scratch = static_cast<float*>(ptr);
+        nd.ready = true;
+    }
+    *out = &nd;
+    return FR_OK;
+}
+
+}  // namespace
+
+extern "C" int fr_decode_attn_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                      void* out, int num_heads, int num_kv_heads, int head_dim,
+                                      int kv_len, void* stream) {
+    if (!q || !k_cache || !v_cache || !out || kv_len <= 0) return FR_ERR_INVALID_ARG;
+    int rc = check_heads(num_heads, num_kv_heads, head_dim);
+    if (rc != FR_OK) return rc;
+    if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 4) || !aligned(out, 4))
+        return FR_ERR_MISALIGNED;
+    NoAllocDevice* nd = nullptr;
+    rc = noalloc_setup(&nd);
+    if (rc != FR_OK) return rc;
+    const int group = num_heads / num_kv_heads;
+    Plan pl;
+    rc = plan_for(&nd->st, head_dim, 1, num_kv_heads, group, kv_len, 1, &pl);
+    if (rc != FR_OK) return rc;
+    // Same plan as fr_decode_attn; a plan whose partials do not fit is refused.
+    if (pl.num_splits > 1 &&
+        partial_bytes(num_heads, pl.num_splits, head_dim) > (size_t)FR_NOALLOC_SCRATCH_BYTES)
+        return FR_ERR_SCRATCH_LIMIT;
+    DecodeParams p = base_params(q, num_heads, num_kv_heads);
+    rc = encode_pair(&p, k_cache, v_cache, head_dim, num_kv_heads, kv_len);
+    if (rc != FR_OK) return rc;
+    p.kv_len = kv_len;
+    p.G = group;
+    p.split_len = pl.split_len;
+    p.num_splits = pl.num_splits;
+    p.head_groups = pl.head_groups;
+    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+    p.err = nullptr;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    __half* o = static_cast<__half*>(out);
+    const bool direct = pl.num_splits == 1;
+    if (direct) {
+        p.write_final = 1;
+        p.out = o;
+    } else {
+        // Every CTA overwrites its own partial state, so nothing in the
+        // scratch needs clearing between calls.
+        p.write_final = 0;
+        p.part_ml = nd->scratch;
+        p.part_acc = nd->scratch + (size_t)num_heads * pl.num_splits * 2;
+    }
+    dim3 grid(pl.num_splits, p.Hkv * pl.head_groups, 1);
+    if (head_dim == 64)
+        rc = pl.nt == 1 ? launch_split<64, 1>(p, grid, s) : launch_split<64, 2>(p, grid, s);
+    else
+        rc = pl.nt == 1 ? launch_split<128, 1>(p, grid, s) : launch_split<128, 2>(p, grid, s);
+    if (rc != FR_OK || direct) return rc;
+    const fr::MergeStrides ms{2LL * pl.num_splits, 2, (long long)pl.num_splits * head_dim,
+                              head_dim};
+    return head_dim == 64 ? launch_merge<64>(p.part_ml, p.part_acc, pl.num_splits, ms, num_heads, o,
+                                             nullptr, nullptr, 0, s)
+                          : launch_merge<128>(p.part_ml, p.part_acc, pl.num_splits, ms, num_heads,
+                                              o, nullptr, nullptr, 0, s);
+}

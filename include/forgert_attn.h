@@ -46,6 +46,10 @@ extern "C" {
 #define FR_ERR_CUDA 4          /* a CUDA runtime call failed: see fr_last_cuda_error() */
 #define FR_ERR_TIMEOUT 5       /* a bounded in-kernel wait ran out (fr_get_device_error) */
 #define FR_ERR_WORKSPACE 6     /* workspace too small while a stream is capturing */
+#define FR_ERR_SCRATCH_LIMIT 7 /* fr_decode_attn_noalloc: partials exceed its static scratch */
+
+/* Size of the static device scratch used by fr_decode_attn_noalloc (2 MiB). */
+#define FR_NOALLOC_SCRATCH_BYTES (2u << 20)
 
 /* Single-token decode attention over kv_len cached positions.
  * Replaces decode_attn_v4_flash (kernels/attention.cuh:65-71; definition
@@ -53,6 +57,28 @@ extern "C" {
  * sqrt(D)) . V in fp16, fp32 accumulation.  kv_len must be >= 1. */
 FR_API int fr_decode_attn(const void* q, const void* k_cache, const void* v_cache, void* out,
                    int num_heads, int num_kv_heads, int head_dim, int kv_len, void* stream);
+
+/* fr_decode_attn without any device allocation, for callers that cannot
+ * call cudaMalloc: code running under another framework's allocator or
+ * memory pool, plugins whose host owns every device allocation, processes
+ * that must not grow their device footprint after start-up.  No counterpart
+ * in the reference (its launchers need no scratch: one CTA per head, no KV
+ * split).  Same arguments, results and split plan as fr_decode_attn; the
+ * split partial states go to a static 2 MiB device array
+ * (FR_NOALLOC_SCRATCH_BYTES) that every GPU loading the library holds until
+ * exit.  A call whose partials need more returns FR_ERR_SCRATCH_LIMIT: the
+ * need is num_heads * splits * (head_dim + 2) * 4 bytes, e.g. 0.8 MB for
+ * 12 heads at kv_len 16384 and 1.1 MB for 28 heads at kv_len 131072, while
+ * 32 heads / 2 kv heads / head_dim 128 at kv_len 16384 (2.1 MB) is refused.
+ * The first call on a device does a one-time set-up (looks up the array's
+ * device address, sets kernel attributes): make that first call before any
+ * stream capture.  All calls on a device share the one array, so calls that
+ * overlap on the GPU (different streams, no ordering) race; serialise them.
+ * In-kernel wait timeouts still end the kernel but are not recorded for
+ * fr_get_device_error. */
+FR_API int fr_decode_attn_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                  void* out, int num_heads, int num_kv_heads, int head_dim,
+                                  int kv_len, void* stream);
 
 /* Batched, ragged decode over a KV pool: sequence b's cache rows are pool
  * rows [row_offsets[b], row_offsets[b] + kv_lens[b]) of
