@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of graphs")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="disable launch overlap (pre-wait K/V prefetch under PDL)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling run: few steps, no clocks/e2e/cpu legs")
@@ -243,6 +245,9 @@ def run_ours(args, torch, dist, rank, local_rank, world):
         raise SystemExit(f"workload {args.workload} not implemented yet")
     wl = Cfg2(torch, rank, device)
     stream = torch.cuda.Stream(device)
+    # Decode-step launch overlap: the attention kernel may stream K/V rows
+    # older than the newest one while the preceding kernel finishes.
+    lib.fr_set_launch_overlap(0 if args.no_overlap else 1)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     A.reserve_workspace(wl.workspace_bytes(A))
     torch.cuda.synchronize()
@@ -363,8 +368,8 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     dom = str(max(wl.groups))
     tr = traffic_per_launch()
     roofline = {
-        "bound": "hbm", "kernel": "split_decode_kernel + lse_merge_kernel (one fr_decode_attn "
-                                  f"call, kv_len {dom})",
+        "bound": "hbm",
+        "kernel": f"split_decode_kernel (one fr_decode_attn call, merge fused), kv_len {dom}",
         "achieved": sweep[dom]["gbs"], "peak": peak, "unit": "GB/s",
         "frac": round(sweep[dom]["gbs"] / peak, 4), "peak_kind": peak_kind,
         "traffic": tr.get("dram_bytes_per_launch") if tr else None,
@@ -372,7 +377,7 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     }
     cfg = wl.config()
     cfg.update({"parallelism": f"dp{world} (one sequence per GPU)", "graph": use_graph,
-                "sweep": sweep})
+                "launch_overlap": not args.no_overlap, "sweep": sweep})
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(max_ms / K, 5), "higher_is_better": True,

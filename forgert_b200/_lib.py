@@ -43,6 +43,7 @@ SIGNATURES = {
     "fr_status_string": (ctypes.c_char_p, [_i]),
     "fr_version": (_i, []),
     "fr_launch_count": (ctypes.c_ulonglong, []),
+    "fr_set_launch_overlap": (_i, [_i]),
 }
 
 

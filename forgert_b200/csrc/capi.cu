@@ -15,6 +15,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -29,8 +30,13 @@ constexpr int kTile = 64;         // KV positions per pipeline stage
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);
 
+constexpr int kClusterCtas = 8;         // cluster size of the fused merge
+constexpr int kMaxUnits = 1 << 16;      // fused-merge counters kept per device
+constexpr size_t kCounterBytes = size_t(kMaxUnits) * sizeof(int);
+
 thread_local int t_last_cuda = 0;
 std::atomic<unsigned long long> g_launches{0};   // kernels launched (or captured) by this library
+std::atomic<int> g_overlap{0};                   // fr_set_launch_overlap
 
 int cuda_fail(cudaError_t e) {
     t_last_cuda = static_cast<int>(e);
@@ -90,6 +96,9 @@ int ensure_workspace(DeviceState* st, size_t bytes, cudaStream_t s) {
     const size_t grow = bytes + bytes / 4;
     cudaError_t e = cudaMalloc(&st->ws, grow);
     if (e != cudaSuccess) { st->ws = nullptr; return cuda_fail(e); }
+    // The fused merge's counters (start of the buffer) must be zero between calls.
+    e = cudaMemset(st->ws, 0, std::min(grow, kCounterBytes));
+    if (e != cudaSuccess) return cuda_fail(e);
     st->ws_bytes = grow;
     return FR_OK;
 }
@@ -143,34 +152,71 @@ template <> struct Stages<128> { static constexpr int value = 3; };
 template <int D, int NT>
 constexpr int kernel_slot() { return (D == 64 ? 0 : 2) + (NT - 1); }
 
+template <int D, int NT, int CL>
+auto kernel_ptr() {
+    return fr::split_decode_kernel<D, NT, kTile, Stages<D>::value, kConsumerWarps, CL>;
+}
+
 template <int D, int NT>
 int prepare_kernel(DeviceState* st) {
-    constexpr int STG = Stages<D>::value;
-    using Smem = fr::SplitSmem<D, NT, kTile, STG, kConsumerWarps>;
-    auto kern = fr::split_decode_kernel<D, NT, kTile, STG, kConsumerWarps>;
+    using Smem = fr::SplitSmem<D, NT, kTile, Stages<D>::value, kConsumerWarps>;
     constexpr int slot = kernel_slot<D, NT>();
     if (!(st->attr_done & (1u << slot))) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(kernel_ptr<D, NT, 1>(),
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(Smem::kBytes));
         if (e != cudaSuccess) return cuda_fail(e);
+        e = cudaFuncSetAttribute(kernel_ptr<D, NT, kClusterCtas>(),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(Smem::kBytes));
+        if (e != cudaSuccess) return cuda_fail(e);
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, Smem::kBytes);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel_ptr<D, NT, 1>(), kThreads,
+                                                          Smem::kBytes);
         st->occupancy[slot] = (e == cudaSuccess && n > 0) ? n : 1;
         st->attr_done |= (1u << slot);
     }
     return FR_OK;
 }
 
-template <int D, int NT>
-int launch_split(const DecodeParams& p, dim3 grid, cudaStream_t s) {
-    constexpr int STG = Stages<D>::value;
-    using Smem = fr::SplitSmem<D, NT, kTile, STG, kConsumerWarps>;
-    auto kern = fr::split_decode_kernel<D, NT, kTile, STG, kConsumerWarps>;
-    kern<<<grid, kThreads, Smem::kBytes, s>>>(p);
+// Launch with optional cluster shape and programmatic dependent launch.
+template <int D, int NT, int CL>
+int launch_split(const DecodeParams& p, dim3 grid, cudaStream_t s, bool pdl) {
+    using Smem = fr::SplitSmem<D, NT, kTile, Stages<D>::value, kConsumerWarps>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Smem::kBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attrs[2];
+    unsigned n = 0;
+    if (CL > 1) {
+        attrs[n].id = cudaLaunchAttributeClusterDimension;
+        attrs[n].val.clusterDim.x = CL;
+        attrs[n].val.clusterDim.y = 1;
+        attrs[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    if (pdl) {
+        attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = n;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel_ptr<D, NT, CL>(), p);
     g_launches.fetch_add(1, std::memory_order_relaxed);
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return FR_OK;
+}
+
+template <int D>
+int launch_split_any(const DecodeParams& p, int nt, int cl, dim3 grid, cudaStream_t s, bool pdl) {
+    if (cl > 1)
+        return nt == 1 ? launch_split<D, 1, kClusterCtas>(p, grid, s, pdl)
+                       : launch_split<D, 2, kClusterCtas>(p, grid, s, pdl);
+    return nt == 1 ? launch_split<D, 1, 1>(p, grid, s, pdl) : launch_split<D, 2, 1>(p, grid, s, pdl);
 }
 
 struct Plan {
@@ -200,11 +246,21 @@ Plan make_plan(int sm_count, int occ, int batch, int num_kv_heads, int group, in
 
 template <int D>
 int launch_merge(const float* ml, const float* acc, int num_states, fr::MergeStrides st, int rows,
-                 __half* out, float* out_ml, float* out_acc, int mode, cudaStream_t s) {
-    fr::lse_merge_kernel<D><<<rows, 32 * fr::kMergeWarps, 0, s>>>(ml, acc, num_states, st, out,
-                                                                  out_ml, out_acc, mode);
+                 __half* out, float* out_ml, float* out_acc, int mode, cudaStream_t s,
+                 bool pdl = false) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows, 1, 1);
+    cfg.blockDim = dim3(32 * fr::kMergeWarps, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fr::lse_merge_kernel<D>, ml, acc, num_states, st, out,
+                                       out_ml, out_acc, mode);
     g_launches.fetch_add(1, std::memory_order_relaxed);
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return FR_OK;
 }
@@ -219,21 +275,44 @@ int check_heads(int num_heads, int num_kv_heads, int head_dim) {
     return FR_OK;
 }
 
+// Tuning knobs (read once): FORGERT_SLOTS_PER_SM caps the CTAs per SM the
+// planner fills (default: the occupancy limit); FORGERT_CLUSTER_MIN_SPLITS is
+// the split count from which the fused merge uses clusters (default 2, 0 =
+// never).
+int env_int(const char* name, int dflt) {
+    const char* v = std::getenv(name);
+    return (v && *v) ? std::atoi(v) : dflt;
+}
+
+int slots_per_sm(int occ) {
+    static const int cap = env_int("FORGERT_SLOTS_PER_SM", 0);
+    return cap > 0 ? std::min(cap, occ) : occ;
+}
+
+int cluster_min_splits() {
+    static const int v = env_int("FORGERT_CLUSTER_MIN_SPLITS", 2);
+    return v;
+}
+
 int plan_for(DeviceState* st, int head_dim, int batch, int num_kv_heads, int group,
              int max_kv_len, int waves, Plan* pl) {
     const int nt = group <= 8 ? 1 : 2;
     int rc = head_dim == 64 ? (nt == 1 ? prepare_kernel<64, 1>(st) : prepare_kernel<64, 2>(st))
                             : (nt == 1 ? prepare_kernel<128, 1>(st) : prepare_kernel<128, 2>(st));
     if (rc != FR_OK) return rc;
-    const int occ = st->occupancy[head_dim == 64 ? (nt - 1) : (2 + nt - 1)];
+    const int occ = slots_per_sm(st->occupancy[head_dim == 64 ? (nt - 1) : (2 + nt - 1)]);
     *pl = make_plan(st->sm_count, occ, batch, num_kv_heads, group, max_kv_len, waves);
     return FR_OK;
 }
 
 // Shared driver of the decode-family entry points.  `p` carries the tensor
 // maps and the sequence geometry.
-//   final_out != nullptr : write fp16 output (merging splits if needed)
+//   final_out != nullptr : write fp16 output
 //   state_ml  != nullptr : write one merged (m, l, acc) state per head row
+// Splits are merged inside the split kernel (clusters of kClusterCtas CTAs
+// through DSMEM, then the last cluster per kv head); a second launch is
+// needed only when there are more (b, kv head, head group) units than
+// counters.
 int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* final_out,
                float* state_ml, float* state_acc, int waves, cudaStream_t s) {
     DeviceState* st = nullptr;
@@ -244,37 +323,47 @@ int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* 
     Plan pl;
     rc = plan_for(st, D, batch, p.Hkv, group, max_kv_len, waves, &pl);
     if (rc != FR_OK) return rc;
+    const long long units = (long long)batch * p.Hkv * pl.head_groups;
+    const int cmin = cluster_min_splits();
+    const int cl = (cmin > 0 && pl.num_splits >= cmin) ? kClusterCtas : 1;
+    const bool fused = units * cl <= kMaxUnits;      // one counter per (unit, cluster rank)
+    const int splits = (pl.num_splits + cl - 1) / cl * cl;     // padded splits are empty
     p.G = group;
     p.split_len = pl.split_len;
-    p.num_splits = pl.num_splits;
+    p.num_splits = splits;
     p.head_groups = pl.head_groups;
     p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
     p.err = st->err;
+    const bool pdl = s != nullptr;
     const long long rows = (long long)batch * p.H;
-    const bool direct = final_out != nullptr && pl.num_splits == 1;
-    if (direct) {
+    if (final_out && splits == 1) {
         p.write_final = 1;
         p.out = final_out;
     } else {
-        rc = ensure_workspace(st, partial_bytes(rows, pl.num_splits, D), s);
+        const int slots = fused ? splits / cl : splits;
+        rc = ensure_workspace(st, kCounterBytes + partial_bytes(rows, slots, D), s);
         if (rc != FR_OK) return rc;
-        p.write_final = 0;
-        p.part_ml = static_cast<float*>(st->ws);
-        p.part_acc = p.part_ml + rows * pl.num_splits * 2;
+        p.part_slots = slots;
+        p.part_ml = reinterpret_cast<float*>(static_cast<char*>(st->ws) + kCounterBytes);
+        p.part_acc = p.part_ml + rows * slots * 2;
+        if (fused) {
+            p.counters = static_cast<int*>(st->ws);
+            p.out = final_out;
+            p.out_ml = state_ml;
+            p.out_acc = state_acc;
+        }
     }
-    dim3 grid(pl.num_splits, p.Hkv * pl.head_groups, batch);
-    if (D == 64)
-        rc = pl.nt == 1 ? launch_split<64, 1>(p, grid, s) : launch_split<64, 2>(p, grid, s);
-    else
-        rc = pl.nt == 1 ? launch_split<128, 1>(p, grid, s) : launch_split<128, 2>(p, grid, s);
-    if (rc != FR_OK || direct) return rc;
+    dim3 grid(splits, p.Hkv * pl.head_groups, batch);
+    rc = D == 64 ? launch_split_any<64>(p, pl.nt, cl, grid, s, pdl)
+                 : launch_split_any<128>(p, pl.nt, cl, grid, s, pdl);
+    if (rc != FR_OK || p.write_final || p.counters) return rc;
+    // unfused: a separate merge launch
     const int mode = final_out ? 0 : 1;
-    // split partials: state (r, s) at index r*num_splits + s
-    const fr::MergeStrides ms{2LL * pl.num_splits, 2, (long long)pl.num_splits * D, D};
-    return D == 64 ? launch_merge<64>(p.part_ml, p.part_acc, pl.num_splits, ms, (int)rows,
-                                      final_out, state_ml, state_acc, mode, s)
-                   : launch_merge<128>(p.part_ml, p.part_acc, pl.num_splits, ms, (int)rows,
-                                       final_out, state_ml, state_acc, mode, s);
+    const fr::MergeStrides ms{2LL * splits, 2, (long long)splits * D, D};
+    return D == 64 ? launch_merge<64>(p.part_ml, p.part_acc, splits, ms, (int)rows, final_out,
+                                      state_ml, state_acc, mode, s, pdl)
+                   : launch_merge<128>(p.part_ml, p.part_acc, splits, ms, (int)rows, final_out,
+                                       state_ml, state_acc, mode, s, pdl);
 }
 
 DecodeParams base_params(const void* q, int num_heads, int num_kv_heads) {
@@ -309,6 +398,9 @@ int fr_decode_attn(const void* q, const void* k_cache, const void* v_cache, void
     rc = encode_pair(&p, k_cache, v_cache, head_dim, num_kv_heads, kv_len);
     if (rc != FR_OK) return rc;
     p.kv_len = kv_len;
+    // Launch overlap: every row but the newest was written before the
+    // preceding kernel ran, so it may stream in before the dependency wait.
+    if (g_overlap.load(std::memory_order_relaxed) && stream) p.prefetch_rows = kv_len - 1;
     return run_decode(p, head_dim, 1, kv_len, static_cast<__half*>(out), nullptr, nullptr, 1,
                       static_cast<cudaStream_t>(stream));
 }
@@ -459,8 +551,8 @@ size_t fr_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int 
         plan_for(st, head_dim, batch, num_kv_heads, group, std::max(1, max_kv_len), 4, &pl4) !=
             FR_OK)
         return 0;
-    const int splits = std::max(pl1.num_splits, pl4.num_splits);
-    return partial_bytes((long long)batch * num_heads, splits, head_dim);
+    const int splits = std::max(pl1.num_splits, pl4.num_splits) + kClusterCtas;
+    return kCounterBytes + partial_bytes((long long)batch * num_heads, splits, head_dim);
 }
 
 int fr_get_device_error(int clear, int* device_code) {
@@ -475,6 +567,11 @@ int fr_get_device_error(int clear, int* device_code) {
     if (clear && code) {
         e = cudaMemset(st->err, 0, sizeof(int));
         if (e != cudaSuccess) return cuda_fail(e);
+        // an aborted call may have left fused-merge counters behind
+        if (st->ws) {
+            e = cudaMemset(st->ws, 0, std::min(st->ws_bytes, kCounterBytes));
+            if (e != cudaSuccess) return cuda_fail(e);
+        }
     }
     if (device_code) *device_code = code;
     return code ? FR_ERR_TIMEOUT : FR_OK;
@@ -499,6 +596,8 @@ const char* fr_status_string(int status) {
 }
 
 int fr_version(void) { return kVersion; }
+
+int fr_set_launch_overlap(int enable) { return g_overlap.exchange(enable ? 1 : 0); }
 
 unsigned long long fr_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
@@ -599,11 +698,10 @@ extern "C" int fr_decode_attn_noalloc(const void* q, const void* k_cache, const 
         p.part_ml = nd->scratch;
         p.part_acc = nd->scratch + (size_t)num_heads * pl.num_splits * 2;
     }
+    p.part_slots = pl.num_splits;
     dim3 grid(pl.num_splits, p.Hkv * pl.head_groups, 1);
-    if (head_dim == 64)
-        rc = pl.nt == 1 ? launch_split<64, 1>(p, grid, s) : launch_split<64, 2>(p, grid, s);
-    else
-        rc = pl.nt == 1 ? launch_split<128, 1>(p, grid, s) : launch_split<128, 2>(p, grid, s);
+    rc = head_dim == 64 ? launch_split_any<64>(p, pl.nt, 1, grid, s, false)
+                        : launch_split_any<128>(p, pl.nt, 1, grid, s, false);
     if (rc != FR_OK || direct) return rc;
     const fr::MergeStrides ms{2LL * pl.num_splits, 2, (long long)pl.num_splits * head_dim,
                               head_dim};

@@ -31,9 +31,11 @@
 // movmatrix.trans, without a shared-memory round trip.
 //
 // Output: with one split the CTA normalises and writes fp16 directly.  With
-// several, each CTA writes its (m, l, acc[D]) partial state and
-// `lse_merge_kernel` combines the splits (the flash-decoding log-sum-exp
-// merge).
+// several, the CTAs of a thread-block cluster merge their (m, l, acc[D])
+// states through distributed shared memory and the last cluster of each
+// (sequence, kv head) merges the cluster partials (the flash-decoding
+// log-sum-exp merge, fused into the same kernel); `lse_merge_kernel` is the
+// separate-launch form of the same merge.
 #pragma once
 #include "fr_ptx.cuh"
 #include <cuda.h>
@@ -53,6 +55,9 @@ struct DecodeParams {
     int causal;                  // 1: sequence b attends to positions [0, b + 1 + causal_offset)
     int causal_offset;
     int zero_tail;               // 1: rows past a sequence's end may hold non-finite data
+    int prefetch_rows;           // rows [0, prefetch_rows) may be loaded before the grid
+                                 // dependency wait (they are not written by the preceding
+                                 // kernels); 0 = everything waits
     int H, Hkv, G;               // query heads, kv heads, group size H / Hkv
     int split_len;               // positions per split (multiple of TILE)
     int num_splits;              // gridDim.x
@@ -60,8 +65,13 @@ struct DecodeParams {
     float scale_log2;            // log2(e) / sqrt(D)
     int write_final;             // 1: single split, write normalised fp16 to out
     __half* out;                 // [B, H, D]
-    float* part_ml;              // [B, H, num_splits, 2] : (m in log2 units, l)
-    float* part_acc;             // [B, H, num_splits, D] : unnormalised accumulators
+    float* out_ml;               // non-null: write merged states (m, l) [B*H, 2] instead of out
+    float* out_acc;              //           and acc [B*H, D]
+    float* part_ml;              // partial states, slot (row * part_slots + j): (m, l)
+    float* part_acc;             //                                            acc[D]
+    int part_slots;              // slots per row: num_splits (unfused) or num_splits / CL
+    int* counters;               // fused merge: one per (b, kv head, head group), zero
+                                 // between calls; nullptr = unfused (lse_merge_kernel follows)
     int* err;                    // device error word
 };
 
@@ -97,8 +107,11 @@ struct SplitSmem {
     static constexpr size_t kBytes = 1024 + kRingBytes + 2 * STAGES * sizeof(uint64_t);
     // Cross-warp merge area (reuses the ring once every tile is consumed).
     static constexpr size_t kMergeBytes =
-        size_t(NW) * (NT * 8) * D * sizeof(float) + size_t(NW) * (NT * 8) * 2 * sizeof(float);
-    static_assert(kMergeBytes <= kRingBytes, "merge area must fit in the ring");
+        size_t(NW) * (NT * 8) * D * sizeof(float) + size_t(NW) * (NT * 8) * 3 * sizeof(float);
+    // CTA state (acc [GP][D], m [GP], l [GP], flag) read by the cluster through DSMEM.
+    static constexpr size_t kStateOffset = (kMergeBytes + 127) / 128 * 128;
+    static constexpr size_t kStateBytes = size_t(NT * 8) * (D + 2) * sizeof(float) + 16;
+    static_assert(kStateOffset + kStateBytes <= kRingBytes, "merge areas must fit in the ring");
     static_assert(kSubBytes % 1024 == 0, "swizzled boxes must stay 1024-byte aligned");
 };
 
@@ -113,14 +126,32 @@ __device__ __forceinline__ uint32_t swz_offset(int r, int col) {
 
 // ---------------------------------------------------------------------------
 // Split-KV decode kernel.
-//   grid  = (num_splits, Hkv * head_groups, B)
+//   grid  = (num_splits, Hkv * head_groups, B), clusters of CL CTAs along x
 //   block = 32 * (NW + 1): NW consumer warps + 1 producer warp
+//
+// Output paths (chosen by the host, uniform over the grid):
+//   write_final        one split: the CTA writes fp16 out directly;
+//   counters == null   unfused: each CTA writes its partial state to slot
+//                      `split`; lse_merge_kernel runs next;
+//   counters != null   fused: the CL CTAs of a cluster merge their states
+//                      through distributed shared memory; with one cluster
+//                      per (b, kv head, head group) that is the output,
+//                      otherwise each cluster writes one partial and the last
+//                      cluster to finish (atomic counter) merges them.
+// With out_ml/out_acc set, the final result is a merged (m, l, acc) state
+// instead of fp16 (used when KV ranges are split across GPUs).
+//
+// Launch overlap: the kernel lets the next grid launch at once
+// (griddepcontrol.launch_dependents) and waits for the preceding grid
+// (griddepcontrol.wait) before it reads q or writes anything; K/V tiles of
+// rows below prefetch_rows may stream in before that wait.
 // ---------------------------------------------------------------------------
-template <int D, int NT, int TILE, int STAGES, int NW>
+template <int D, int NT, int TILE, int STAGES, int NW, int CL>
 __global__ void __launch_bounds__(32 * (NW + 1))
 split_decode_kernel(const __grid_constant__ DecodeParams p) {
     static_assert(D % 64 == 0, "head_dim must be a multiple of 64");
     static_assert(TILE == 16 * NW, "each consumer warp owns one 16-row m-tile per stage");
+    static_assert(CL >= 1 && CL <= 16, "cluster size");
     using S = SplitSmem<D, NT, TILE, STAGES, NW>;
     constexpr int GP = NT * 8;          // padded heads per CTA
     constexpr int KSTEPS = D / 16;      // k-steps of the QK product
@@ -133,6 +164,10 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     unsigned char* vring = smem + STAGES * S::kTileBytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
     uint64_t* empty = full + STAGES;
+    float* st_acc = reinterpret_cast<float*>(smem + S::kStateOffset);   // [GP][D]
+    float* st_m = st_acc + GP * D;                                       // [GP]
+    float* st_l = st_m + GP;                                             // [GP]
+    uint32_t* st_flag = reinterpret_cast<uint32_t*>(st_l + GP);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -152,6 +187,9 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     const int pos_end = min(seq_len, pos_begin + p.split_len);
     const int ntiles = pos_end > pos_begin ? (pos_end - pos_begin + TILE - 1) / TILE : 0;
 
+    // Every CTA of this grid is running: the next grid may start launching.
+    grid_launch_dependents();
+
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
@@ -161,13 +199,20 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     }
     __syncthreads();
 
-    // ------------------------------------------------------------ producer
+    bool ok = true;
+    const int g = lane >> 2;     // fragment row group
+    const int t = lane & 3;      // fragment column pair
+    float o[DTILES][NT][4];
+    float m_run[NT][2], l_run[NT][2];
+
     if (warp == NW) {
-        int issued = 0;
+        // -------------------------------------------------------- producer
         if (lane == 0 && ntiles > 0) {
             prefetch_tensormap(&p.kmap);
             prefetch_tensormap(&p.vmap);
             const uint64_t policy = l2_policy_evict_first();
+            bool waited = false;
+            int issued = 0;
             for (int i = 0; i < ntiles; ++i) {
                 const int s = i % STAGES;
                 if (i >= STAGES) {
@@ -176,7 +221,12 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                         break;
                     }
                 }
-                const int row = int(row_base + pos_begin + i * TILE);
+                const int t0 = pos_begin + i * TILE;
+                if (!waited && t0 + TILE > p.prefetch_rows) {
+                    grid_dependency_wait();
+                    waited = true;
+                }
+                const int row = int(row_base + t0);
                 mbar_arrive_expect_tx(&full[s], uint32_t(2 * S::kTileBytes));
 #pragma unroll
                 for (int sub = 0; sub < S::kSub; ++sub) {
@@ -188,7 +238,8 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                 ++issued;
             }
             // Drain: wait until every copy this CTA issued has landed, so no
-            // TMA write is still in flight when the CTA retires.
+            // TMA write is still in flight when the ring is reused or the CTA
+            // retires.
             for (int i = max(0, issued - STAGES); i < issued; ++i) {
                 if (!mbar_wait_bounded(&full[i % STAGES], (i / STAGES) & 1)) {
                     record_error(p.err, kDevTimeoutFull);
@@ -196,236 +247,381 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                 }
             }
         }
-        return;
-    }
+        __syncwarp();
+    } else {
+        // -------------------------------------------------------- consumers
+        // q (and everything this CTA writes) depends on the preceding grid.
+        grid_dependency_wait();
 
-    // ------------------------------------------------------------ consumers
-    const int g = lane >> 2;     // fragment row group
-    const int t = lane & 3;      // fragment column pair
-
-    // Q^T as the B operand of S^T = K Q^T: b0 = Q[head][ks*16 + 2t .. +1], b1 = +8.
-    uint32_t qb[KSTEPS][NT][2];
-    {
-        const __half* qrow_base = p.q + ((size_t)b * p.H + h0) * D;
+        // Q^T as the B operand of S^T = K Q^T: b0 = Q[head][ks*16 + 2t .. +1], b1 = +8.
+        uint32_t qb[KSTEPS][NT][2];
+        {
+            const __half* qrow_base = p.q + ((size_t)b * p.H + h0) * D;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int hj = nt * 8 + g;
-            const bool valid = hj < gcount;
-            const __half* qrow = qrow_base + (size_t)hj * D;
+            for (int nt = 0; nt < NT; ++nt) {
+                const int hj = nt * 8 + g;
+                const bool valid = hj < gcount;
+                const __half* qrow = qrow_base + (size_t)hj * D;
 #pragma unroll
-            for (int ks = 0; ks < KSTEPS; ++ks) {
-                qb[ks][nt][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * t) : 0u;
-                qb[ks][nt][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * t) : 0u;
-            }
-        }
-    }
-
-    float o[DTILES][NT][4];
-#pragma unroll
-    for (int dm = 0; dm < DTILES; ++dm)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) o[dm][nt][c] = 0.f;
-    float m_run[NT][2], l_run[NT][2];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        m_run[nt][0] = m_run[nt][1] = -INFINITY;
-        l_run[nt][0] = l_run[nt][1] = 0.f;
-    }
-
-    const float sl2 = p.scale_log2;
-    bool ok = true;
-    // ldmatrix rows/columns of this lane (see the fragment maps in the file header).
-    const int row0 = warp * 16;
-    const int k_row = row0 + (lane & 7) + ((lane >> 3) & 1) * 8;
-    const int k_col = (lane >> 4) * 8;
-    const int v_row = row0 + (lane & 7) + ((lane >> 4) & 1) * 8;
-    const int v_col = ((lane >> 3) & 1) * 8;
-    const uint32_t kring_s = smem_u32(kring);
-    const uint32_t vring_s = smem_u32(vring);
-
-    for (int i = 0; i < ntiles; ++i) {
-        const int s = i % STAGES;
-        if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1)) {
-            record_error(p.err, kDevTimeoutFull);
-            ok = false;
-            break;
-        }
-        const int tpos0 = pos_begin + i * TILE + row0;     // first position of this warp's m-tile
-        if (tpos0 < pos_end) {
-            const uint32_t kst = kring_s + s * S::kTileBytes;
-            const uint32_t vst = vring_s + s * S::kTileBytes;
-            const int valid_rows = pos_end - tpos0;        // rows >= this are past the end
-            bool fenced = false;
-            if (p.zero_tail && valid_rows < 16) {
-                // Rows past the sequence may hold anything (other sequences'
-                // rows of a pool); zero this warp's V rows there so that
-                // P = 0 multiplies finite values.
-                unsigned char* vbase = vring + s * S::kTileBytes;
-                for (int c = lane; c < (16 - valid_rows) * S::kSub * 8; c += 32) {
-                    const int r = row0 + valid_rows + c / (S::kSub * 8);
-                    const int rest = c % (S::kSub * 8);
-                    *reinterpret_cast<uint4*>(vbase + (rest >> 3) * S::kSubBytes + r * 128 +
-                                              (rest & 7) * 16) = make_uint4(0, 0, 0, 0);
+                for (int ks = 0; ks < KSTEPS; ++ks) {
+                    qb[ks][nt][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * t) : 0u;
+                    qb[ks][nt][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * t) : 0u;
                 }
-                __syncwarp();
-                fenced = true;
             }
+        }
 
-            // ---- S^T = K Q^T (16 positions x GP heads)
-            float sacc[NT][4];
+#pragma unroll
+        for (int dm = 0; dm < DTILES; ++dm)
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
+                for (int c = 0; c < 4; ++c) o[dm][nt][c] = 0.f;
 #pragma unroll
-            for (int ks = 0; ks < KSTEPS; ++ks) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4(a0, a1, a2, a3, kst + swz_offset<TILE>(k_row, ks * 16 + k_col));
+        for (int nt = 0; nt < NT; ++nt) {
+            m_run[nt][0] = m_run[nt][1] = -INFINITY;
+            l_run[nt][0] = l_run[nt][1] = 0.f;
+        }
+
+        const float sl2 = p.scale_log2;
+        // ldmatrix rows/columns of this lane (see the fragment maps in the file header).
+        const int row0 = warp * 16;
+        const int k_row = row0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int k_col = (lane >> 4) * 8;
+        const int v_row = row0 + (lane & 7) + ((lane >> 4) & 1) * 8;
+        const int v_col = ((lane >> 3) & 1) * 8;
+        const uint32_t kring_s = smem_u32(kring);
+        const uint32_t vring_s = smem_u32(vring);
+
+        for (int i = 0; i < ntiles; ++i) {
+            const int s = i % STAGES;
+            if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1)) {
+                record_error(p.err, kDevTimeoutFull);
+                ok = false;
+                break;
+            }
+            const int tpos0 = pos_begin + i * TILE + row0;     // first position of this warp's m-tile
+            if (tpos0 < pos_end) {
+                const uint32_t kst = kring_s + s * S::kTileBytes;
+                const uint32_t vst = vring_s + s * S::kTileBytes;
+                const int valid_rows = pos_end - tpos0;        // rows >= this are past the end
+                bool fenced = false;
+                if (p.zero_tail && valid_rows < 16) {
+                    // Rows past the sequence may hold anything (other sequences'
+                    // rows of a pool); zero this warp's V rows there so that
+                    // P = 0 multiplies finite values.
+                    unsigned char* vbase = vring + s * S::kTileBytes;
+                    for (int c = lane; c < (16 - valid_rows) * S::kSub * 8; c += 32) {
+                        const int r = row0 + valid_rows + c / (S::kSub * 8);
+                        const int rest = c % (S::kSub * 8);
+                        *reinterpret_cast<uint4*>(vbase + (rest >> 3) * S::kSubBytes + r * 128 +
+                                                  (rest & 7) * 16) = make_uint4(0, 0, 0, 0);
+                    }
+                    __syncwarp();
+                    fenced = true;
+                }
+
+                // ---- S^T = K Q^T (16 positions x GP heads)
+                float sacc[NT][4];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
-                    mma_16816(sacc[nt], a0, a1, a2, a3, qb[ks][nt][0], qb[ks][nt][1]);
-            }
-
-            // ---- mask rows past the end of the split
-            const bool row_lo_ok = g < valid_rows;
-            const bool row_hi_ok = g + 8 < valid_rows;
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                if (!row_lo_ok) { sacc[nt][0] = -INFINITY; sacc[nt][1] = -INFINITY; }
-                if (!row_hi_ok) { sacc[nt][2] = -INFINITY; sacc[nt][3] = -INFINITY; }
-            }
-
-            // ---- online softmax per head column (base 2)
-            uint32_t pb[NT][2];
-            uint32_t pl[NT][2];
+                    for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                float alpha[2];
-                float pr[4];
+                for (int ks = 0; ks < KSTEPS; ++ks) {
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(a0, a1, a2, a3, kst + swz_offset<TILE>(k_row, ks * 16 + k_col));
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    float mx = fmaxf(sacc[nt][j], sacc[nt][j + 2]);
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                    const float m_new = fmaxf(m_run[nt][j], mx * sl2);
-                    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-                    alpha[j] = fast_exp2(m_run[nt][j] - m_use);
-                    m_run[nt][j] = m_new;
-                    pr[j] = fast_exp2(fmaf(sacc[nt][j], sl2, -m_use));
-                    pr[j + 2] = fast_exp2(fmaf(sacc[nt][j + 2], sl2, -m_use));
-                    l_run[nt][j] = fmaf(l_run[nt][j], alpha[j], pr[j] + pr[j + 2]);
+                    for (int nt = 0; nt < NT; ++nt)
+                        mma_16816(sacc[nt], a0, a1, a2, a3, qb[ks][nt][0], qb[ks][nt][1]);
                 }
-#pragma unroll
-                for (int dm = 0; dm < DTILES; ++dm) {
-                    o[dm][nt][0] *= alpha[0];
-                    o[dm][nt][1] *= alpha[1];
-                    o[dm][nt][2] *= alpha[0];
-                    o[dm][nt][3] *= alpha[1];
-                }
-                // P^T fragments: rows = positions, cols = heads -> B layout
-                // (k = pos, n = head).  P = P_hi + P_lo, both fp16.
-                const __half2 h01 = __floats2half2_rn(pr[0], pr[1]);
-                const __half2 h23 = __floats2half2_rn(pr[2], pr[3]);
-                pb[nt][0] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h01));
-                pb[nt][1] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h23));
-                if (kSplitP) {
-                    const float2 f01 = __half22float2(h01);
-                    const float2 f23 = __half22float2(h23);
-                    pl[nt][0] = movmatrix_trans(pack_half2(pr[0] - f01.x, pr[1] - f01.y));
-                    pl[nt][1] = movmatrix_trans(pack_half2(pr[2] - f23.x, pr[3] - f23.y));
-                }
-            }
 
-            // ---- O^T += V^T P^T
-#pragma unroll
-            for (int dm = 0; dm < DTILES; ++dm) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4_trans(a0, a1, a2, a3, vst + swz_offset<TILE>(v_row, dm * 16 + v_col));
+                // ---- mask rows past the end of the split
+                const bool row_lo_ok = g < valid_rows;
+                const bool row_hi_ok = g + 8 < valid_rows;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    mma_16816(o[dm][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
-                    if (kSplitP) mma_16816(o[dm][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+                    if (!row_lo_ok) { sacc[nt][0] = -INFINITY; sacc[nt][1] = -INFINITY; }
+                    if (!row_hi_ok) { sacc[nt][2] = -INFINITY; sacc[nt][3] = -INFINITY; }
                 }
+
+                // ---- online softmax per head column (base 2)
+                uint32_t pb[NT][2];
+                uint32_t pl[NT][2];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    float alpha[2];
+                    float pr[4];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        float mx = fmaxf(sacc[nt][j], sacc[nt][j + 2]);
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                        const float m_new = fmaxf(m_run[nt][j], mx * sl2);
+                        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+                        alpha[j] = fast_exp2(m_run[nt][j] - m_use);
+                        m_run[nt][j] = m_new;
+                        pr[j] = fast_exp2(fmaf(sacc[nt][j], sl2, -m_use));
+                        pr[j + 2] = fast_exp2(fmaf(sacc[nt][j + 2], sl2, -m_use));
+                        l_run[nt][j] = fmaf(l_run[nt][j], alpha[j], pr[j] + pr[j + 2]);
+                    }
+#pragma unroll
+                    for (int dm = 0; dm < DTILES; ++dm) {
+                        o[dm][nt][0] *= alpha[0];
+                        o[dm][nt][1] *= alpha[1];
+                        o[dm][nt][2] *= alpha[0];
+                        o[dm][nt][3] *= alpha[1];
+                    }
+                    // P^T fragments: rows = positions, cols = heads -> B layout
+                    // (k = pos, n = head).  P = P_hi + P_lo, both fp16.
+                    const __half2 h01 = __floats2half2_rn(pr[0], pr[1]);
+                    const __half2 h23 = __floats2half2_rn(pr[2], pr[3]);
+                    pb[nt][0] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h01));
+                    pb[nt][1] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h23));
+                    if (kSplitP) {
+                        const float2 f01 = __half22float2(h01);
+                        const float2 f23 = __half22float2(h23);
+                        pl[nt][0] = movmatrix_trans(pack_half2(pr[0] - f01.x, pr[1] - f01.y));
+                        pl[nt][1] = movmatrix_trans(pack_half2(pr[2] - f23.x, pr[3] - f23.y));
+                    }
+                }
+
+                // ---- O^T += V^T P^T
+#pragma unroll
+                for (int dm = 0; dm < DTILES; ++dm) {
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_trans(a0, a1, a2, a3, vst + swz_offset<TILE>(v_row, dm * 16 + v_col));
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        mma_16816(o[dm][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+                        if (kSplitP) mma_16816(o[dm][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+                    }
+                }
+                // Generic-proxy writes into a stage the TMA will refill later.
+                if (fenced) fence_proxy_async_smem();
             }
-            // Generic-proxy writes into a stage the TMA will refill later.
-            if (fenced) fence_proxy_async_smem();
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-    }
-
-    // Row sums: each lane summed its own positions; fold the 8 row groups.
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            float l = l_run[nt][j];
-            l += __shfl_xor_sync(0xffffffffu, l, 4);
-            l += __shfl_xor_sync(0xffffffffu, l, 8);
-            l += __shfl_xor_sync(0xffffffffu, l, 16);
-            l_run[nt][j] = l;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
 
-    // Every consumer must be past its last ldmatrix before the ring is
-    // reused as the merge area.
-    const int ok_all = consumer_sync_and(ok ? 1 : 0, NW * 32);
-    if (!ok_all) return;
-
-    // ---- cross-warp merge through shared memory
-    float* macc = reinterpret_cast<float*>(smem);                 // [NW][GP][D]
-    float* mml = macc + NW * GP * D;                              // [NW][GP][2]
-#pragma unroll
-    for (int dm = 0; dm < DTILES; ++dm)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int d = dm * 16 + g + ((c >> 1) << 3);
-                const int hj = nt * 8 + 2 * t + (c & 1);
-                macc[(warp * GP + hj) * D + d] = o[dm][nt][c];
-            }
-    if (g == 0) {
+        // Row sums: each lane summed its own positions; fold the 8 row groups.
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const int hj = nt * 8 + 2 * t + j;
-                mml[(warp * GP + hj) * 2 + 0] = m_run[nt][j];
-                mml[(warp * GP + hj) * 2 + 1] = l_run[nt][j];
+                float l = l_run[nt][j];
+                l += __shfl_xor_sync(0xffffffffu, l, 4);
+                l += __shfl_xor_sync(0xffffffffu, l, 8);
+                l += __shfl_xor_sync(0xffffffffu, l, 16);
+                l_run[nt][j] = l;
             }
-    }
-    consumer_sync(NW * 32);
 
-    const size_t head_base = (size_t)b * p.H + h0;
-    for (int idx = threadIdx.x; idx < gcount * D; idx += NW * 32) {
-        const int hj = idx / D;
-        const int d = idx % D;
-        float mstar = -INFINITY;
+        // Every consumer must be past its last ldmatrix before the ring is
+        // reused as the merge area.
+        const int ok_all = consumer_sync_and(ok ? 1 : 0, NW * 32);
+
+        // ---- cross-warp merge through shared memory -> CTA state
+        float* macc = reinterpret_cast<float*>(smem);                 // [NW][GP][D]
+        float* mml = macc + NW * GP * D;                              // [NW][GP][2]
+        float* wsc = mml + NW * GP * 2;                               // [GP][NW] warp weights
+        if (ok_all) {
 #pragma unroll
-        for (int w = 0; w < NW; ++w) mstar = fmaxf(mstar, mml[(w * GP + hj) * 2]);
-        const float muse = (mstar == -INFINITY) ? 0.f : mstar;
-        float acc = 0.f, l = 0.f;
+            for (int dm = 0; dm < DTILES; ++dm)
 #pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            const float sc = fast_exp2(mml[(w * GP + hj) * 2] - muse);
-            acc = fmaf(macc[(w * GP + hj) * D + d], sc, acc);
-            l = fmaf(mml[(w * GP + hj) * 2 + 1], sc, l);
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int d = dm * 16 + g + ((c >> 1) << 3);
+                        const int hj = nt * 8 + 2 * t + (c & 1);
+                        macc[(warp * GP + hj) * D + d] = o[dm][nt][c];
+                    }
+            if (g == 0) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int hj = nt * 8 + 2 * t + j;
+                        mml[(warp * GP + hj) * 2 + 0] = m_run[nt][j];
+                        mml[(warp * GP + hj) * 2 + 1] = l_run[nt][j];
+                    }
+            }
         }
-        const size_t hrow = head_base + hj;
-        if (p.write_final) {
-            p.out[hrow * D + d] = __float2half_rn(l > 0.f ? acc / l : 0.f);
-        } else {
-            const size_t pidx = hrow * p.num_splits + split;
-            p.part_acc[pidx * D + d] = acc;
-            if (d == 0) {
-                p.part_ml[pidx * 2 + 0] = mstar;
-                p.part_ml[pidx * 2 + 1] = l;
+        consumer_sync(NW * 32);
+        // One thread per head: the max over warps, each warp's weight, l.
+        if (threadIdx.x < GP) {
+            const int hj = threadIdx.x;
+            float mstar = -INFINITY, l = 0.f;
+            if (ok_all) {
+#pragma unroll
+                for (int w = 0; w < NW; ++w) mstar = fmaxf(mstar, mml[(w * GP + hj) * 2]);
+                const float muse = (mstar == -INFINITY) ? 0.f : mstar;
+#pragma unroll
+                for (int w = 0; w < NW; ++w) {
+                    const float sc = fast_exp2(mml[(w * GP + hj) * 2] - muse);
+                    wsc[hj * NW + w] = sc;
+                    l = fmaf(mml[(w * GP + hj) * 2 + 1], sc, l);
+                }
+            } else {
+#pragma unroll
+                for (int w = 0; w < NW; ++w) wsc[hj * NW + w] = 0.f;
+            }
+            st_m[hj] = mstar;
+            st_l[hj] = l;
+        }
+        consumer_sync(NW * 32);
+
+        const size_t head_base = (size_t)b * p.H + h0;
+        constexpr int kPerThread = GP * D / (NW * 32);
+#pragma unroll
+        for (int it = 0; it < kPerThread; ++it) {
+            const int idx = threadIdx.x + it * NW * 32;
+            const int hj = idx / D;
+            const int d = idx % D;
+            float acc = 0.f;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) acc = fmaf(macc[(w * GP + hj) * D + d], wsc[hj * NW + w], acc);
+            const size_t hrow = head_base + hj;
+            if (p.counters) {
+                st_acc[hj * D + d] = acc;                    // fused: keep the CTA state
+            } else if (hj < gcount && ok_all) {
+                const float l = st_l[hj];
+                if (p.write_final) {
+                    p.out[hrow * D + d] = __float2half_rn(l > 0.f ? acc / l : 0.f);
+                } else {
+                    const size_t slot = hrow * p.part_slots + split;
+                    p.part_acc[slot * D + d] = acc;
+                    if (d == 0) {
+                        p.part_ml[slot * 2 + 0] = st_m[hj];
+                        p.part_ml[slot * 2 + 1] = l;
+                    }
+                }
             }
         }
     }
+
+    if (!p.counters) return;       // unfused / single-split paths end here (uniform)
+    __syncthreads();               // CTA state complete (producer included)
+
+    // ------------------------------------------------------ fused merge
+    // Level 1: the CL CTAs of the cluster merge their states through DSMEM;
+    // CTA rank r merges element slice r of the (gcount x D) output.
+    // Level 2 (several clusters per unit): slice r of every cluster partial is
+    // written only by rank r, so the last rank-r CTA to finish (one counter
+    // per (unit, rank)) merges slice r on its own - no second cluster barrier.
+    const int crank = CL > 1 ? int(cluster_ctarank()) : 0;
+    const int ncl = p.part_slots;                    // clusters per (b, kv head, head group)
+    const int cl_id = split / CL;
+    const size_t head_base = (size_t)b * p.H + h0;
+    const int unit = (b * p.Hkv + kvh) * p.head_groups + hgrp;
+    const int nel = gcount * D;
+    const int per = (nel + CL - 1) / CL;
+    const int e_begin = crank * per;
+    const int e_end = min(nel, e_begin + per);
+    const bool state_out = p.out_ml != nullptr;
+
+    if constexpr (CL > 1) cluster_sync_all();       // every CTA's state is in its smem
+    {
+        const uint32_t acc_s = smem_u32(st_acc), m_s = smem_u32(st_m), l_s = smem_u32(st_l);
+        for (int e = e_begin + threadIdx.x; e < e_end; e += blockDim.x) {
+            const int hj = e / D;
+            const int d = e - hj * D;
+            float mj[CL], lj[CL], aj[CL];
+#pragma unroll
+            for (int j = 0; j < CL; ++j) {
+                if constexpr (CL > 1) {
+                    mj[j] = ld_dsmem_f32(dsmem_addr(m_s + hj * 4, j));
+                    lj[j] = ld_dsmem_f32(dsmem_addr(l_s + hj * 4, j));
+                    aj[j] = ld_dsmem_f32(dsmem_addr(acc_s + (hj * D + d) * 4, j));
+                } else {
+                    mj[j] = st_m[hj];
+                    lj[j] = st_l[hj];
+                    aj[j] = st_acc[hj * D + d];
+                }
+            }
+            float mstar = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < CL; ++j) mstar = fmaxf(mstar, mj[j]);
+            const float muse = (mstar == -INFINITY) ? 0.f : mstar;
+            float a = 0.f, l = 0.f;
+#pragma unroll
+            for (int j = 0; j < CL; ++j) {
+                const float sc = fast_exp2(mj[j] - muse);
+                a = fmaf(aj[j], sc, a);
+                l = fmaf(lj[j], sc, l);
+            }
+            const size_t hrow = head_base + hj;
+            if (ncl == 1) {
+                if (state_out) {
+                    p.out_acc[hrow * D + d] = a;
+                    if (d == 0) { p.out_ml[2 * hrow] = mstar; p.out_ml[2 * hrow + 1] = l; }
+                } else {
+                    p.out[hrow * D + d] = __float2half_rn(l > 0.f ? a / l : 0.f);
+                }
+            } else {
+                const size_t slot = hrow * ncl + cl_id;
+                p.part_acc[slot * D + d] = a;
+                if (d == 0) { p.part_ml[2 * slot] = mstar; p.part_ml[2 * slot + 1] = l; }
+            }
+        }
+    }
+    // This CTA's DSMEM reads are done; peers may retire once everyone arrives
+    // (the matching wait sits at the end, off the critical path).
+    if constexpr (CL > 1) cluster_arrive_release();
+
+    if (ncl > 1) {
+        __syncthreads();                             // slice stores of this CTA are done
+        if (threadIdx.x == 0) {
+            // acq_rel: publishes this CTA's slice (ordered before by the
+            // barrier) and, for the last arriver, acquires the other slices.
+            const int old = atom_add_acq_rel_gpu(&p.counters[unit * CL + crank], 1);
+            st_flag[0] = (old == ncl - 1) ? 1u : 0u;
+        }
+        __syncthreads();
+        if (st_flag[0]) {
+            // Last rank-`crank` CTA: merge slice `crank` of all ncl partials,
+            // every load of a chunk in flight at once.
+            for (int e = e_begin + threadIdx.x; e < e_end; e += blockDim.x) {
+                const int hj = e / D;
+                const int d = e - hj * D;
+                const size_t hrow = head_base + hj;
+                const float* mlp = p.part_ml + 2 * hrow * ncl;
+                const float* accp = p.part_acc + hrow * ncl * D + d;
+                float m = -INFINITY, l = 0.f, a = 0.f;
+                for (int c0 = 0; c0 < ncl; c0 += 8) {
+                    float mv[8], lv[8], av[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const bool in = c0 + u < ncl;
+                        mv[u] = in ? __ldcg(mlp + 2 * (c0 + u)) : -INFINITY;
+                        lv[u] = in ? __ldcg(mlp + 2 * (c0 + u) + 1) : 0.f;
+                        av[u] = in ? __ldcg(accp + (size_t)(c0 + u) * D) : 0.f;
+                    }
+                    float cm = m;
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) cm = fmaxf(cm, mv[u]);
+                    const float mu = (cm == -INFINITY) ? 0.f : cm;
+                    const float r = fast_exp2(m - mu);
+                    a *= r;
+                    l *= r;
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const float w = fast_exp2(mv[u] - mu);
+                        a = fmaf(av[u], w, a);
+                        l = fmaf(lv[u], w, l);
+                    }
+                    m = cm;
+                }
+                if (state_out) {
+                    p.out_acc[hrow * D + d] = a;
+                    if (d == 0) { p.out_ml[2 * hrow] = m; p.out_ml[2 * hrow + 1] = l; }
+                } else {
+                    p.out[hrow * D + d] = __float2half_rn(l > 0.f ? a / l : 0.f);
+                }
+            }
+            if (threadIdx.x == 0) p.counters[unit * CL + crank] = 0;   // ready for the next call
+        }
+    }
+    if constexpr (CL > 1) cluster_wait_acquire();   // peers done reading this CTA's smem
 }
 
 // ---------------------------------------------------------------------------
@@ -454,6 +650,8 @@ lse_merge_kernel(const float* __restrict__ ml, const float* __restrict__ acc, in
     constexpr int VEC = D / 32;
     __shared__ float s_acc[kMergeWarps][D];
     __shared__ float s_m[kMergeWarps], s_l[kMergeWarps];
+    grid_launch_dependents();
+    grid_dependency_wait();          // the partial states come from the preceding grid
     const int r = blockIdx.x;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;

@@ -167,6 +167,16 @@ FR_API int fr_last_cuda_error(void);
 FR_API const char* fr_status_string(int status);
 FR_API int fr_version(void);
 
+/* Launch overlap for fr_decode_attn on a non-default stream: when enabled,
+ * K/V rows [0, kv_len - 1) may be read before the kernel's grid-dependency
+ * wait, i.e. while the preceding kernel in the stream is still running
+ * (programmatic dependent launch).  Enable it only when those rows are never
+ * written by the kernels immediately preceding the call - true for the
+ * reference's decode step, where only row kv_len - 1 is new.  q, the newest
+ * row and every output always wait.  Process-wide, default off; returns the
+ * previous setting.  No reference counterpart. */
+FR_API int fr_set_launch_overlap(int enable);
+
 /* Number of kernels this library has launched (or recorded into a CUDA graph
  * under capture) in this process.  Diagnostics only; no reference
  * counterpart. */

@@ -287,3 +287,62 @@ def test_invalid_arguments_raise():
         A.decode_attn_v4_flash(qd, kd, kd, qd, 8, 2, 64, 0)      # empty cache
     assert e.value.status == 1
     assert A.device_error() == 0
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_overlap_mode_after_rope_append(use_graph):
+    """Decode step as the runtime runs it, on a non-default stream with launch
+    overlap on: the fused prologue appends row kv_len-1 (and rotates q) right
+    before each attention call, which may prefetch only the older rows
+    before its grid-dependency wait.  Four layers back to back."""
+    from forgert_b200 import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(17)
+    L, H, Hkv, D, S, kv = 4, 12, 2, 128, 6000, 5000
+    cos_d, sin_d = A.rope_precompute_tables(S, D, W.ROPE_THETA)
+    ct, st = O.c_rope_tables(S, D, W.ROPE_THETA)
+    caches = [(W.normal_fp16(rng, (S, Hkv, D)), W.normal_fp16(rng, (S, Hkv, D))) for _ in range(L)]
+    qs = [W.normal_fp16(rng, (1, H, D)) for _ in range(L)]
+    knew = [W.normal_fp16(rng, (1, Hkv, D)) for _ in range(L)]
+    vnew = [W.normal_fp16(rng, (1, Hkv, D)) for _ in range(L)]
+    dev_caches = [(dev(k), dev(v)) for k, v in caches]
+    dq = [dev(q) for q in qs]
+    dk = [dev(k) for k in knew]
+    dv = [dev(v) for v in vnew]
+    outs = [torch.full((H, D), float("nan"), dtype=torch.float16, device="cuda") for _ in range(L)]
+    A.reserve_workspace(A.decode_workspace_size(1, H, Hkv, D, kv))
+    s = torch.cuda.Stream()
+    old = lib.fr_set_launch_overlap(1)
+    try:
+        def step(stream):
+            for l in range(L):
+                A.rope_append(dq[l], dk[l], dv[l], dev_caches[l][0], dev_caches[l][1], cos_d, sin_d,
+                              1, H, Hkv, D, kv - 1, stream)
+                A.decode_attn_v4_flash(dq[l], dev_caches[l][0], dev_caches[l][1], outs[l], H, Hkv,
+                                       D, kv, stream)
+        # warm once outside capture (library state), then restore the inputs
+        with torch.cuda.stream(s):
+            step(s)
+        torch.cuda.synchronize()
+        for l in range(L):
+            dq[l].copy_(dev(qs[l]))
+            dk[l].copy_(dev(knew[l]))
+            outs[l].fill_(float("nan"))
+        torch.cuda.synchronize()
+        if use_graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                step(torch.cuda.current_stream())
+            g.replay()
+        else:
+            with torch.cuda.stream(s):
+                step(s)
+        torch.cuda.synchronize()
+    finally:
+        lib.fr_set_launch_overlap(old)
+    assert A.device_error() == 0
+    for l in range(L):
+        qo, ko, kco, vco = O.c_rope_append(qs[l], knew[l], vnew[l], caches[l][0], caches[l][1],
+                                           ct, st, kv - 1)
+        exact = O.decode_f64(qo[0], kco, vco, kv)
+        assert_close(outs[l].cpu().numpy(), exact, what=f"overlap layer {l}")
