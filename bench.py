@@ -222,6 +222,12 @@ class Cfg2:
         n = self.L * len(self.groups)
         return n * per, n * per
 
+    scaling = "weak"
+    graphable = True
+
+    def call_bytes(self, kv: int) -> int:
+        return W.decode_bytes([kv], self.H, self.HKV, self.D)
+
     def config(self):
         return {
             "workload": "cfg2: Qwen2-1.5B-shape decode attention, batch 1 per GPU, "
@@ -234,6 +240,161 @@ class Cfg2:
         }
 
 
+class Cfg3:
+    """Qwen2-7B batched decode: 64 sequences, kv_len ~ U{1024..8192} (seed 2),
+    H28 Hkv4 D128.  The 256 (sequence, kv head) units are assigned to ranks
+    by LPT on token count; each rank keeps its units in one KV pool
+    [rows, 1, 128] (a unit is one kv head with its 7 query heads) and runs one
+    batched call.  Total work is fixed ("strong")."""
+
+    H, HKV, D, G = 28, 4, 128, 7
+    scaling = "strong"
+    graphable = True
+
+    def __init__(self, torch, rank: int, world: int, device):
+        from forgert_b200 import sharding as SH
+        self.torch = torch
+        self.lens_all = W.cfg3_lens()
+        mine = SH.shard_batched(self.lens_all, self.HKV, world)[rank]
+        self.units = mine
+        lens = [u[2] for u in mine]
+        self.U = len(mine)
+        rows = int(sum(lens))
+        offs = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+        g = torch.Generator(device=device)
+        g.manual_seed(2 + 1000 * rank)
+        self.kpool = torch.empty((rows, 1, self.D), dtype=torch.float16, device=device).normal_(generator=g)
+        self.vpool = torch.empty((rows, 1, self.D), dtype=torch.float16, device=device).normal_(generator=g)
+        self.offs = torch.from_numpy(offs).to(device)
+        self.lens = torch.tensor(lens, dtype=torch.int32, device=device)
+        self.q = torch.empty((self.U, self.G, self.D), dtype=torch.float16, device=device).normal_(generator=g)
+        self.out = torch.empty_like(self.q)
+        self.rows = rows
+        self.max_len = int(max(lens))
+        self.groups = ["batch"]
+        self.my_bytes = W.decode_bytes(lens, self.G, 1, self.D)
+        self.q_host = self.q.cpu().pin_memory()
+        self.out_host = torch.empty_like(self.q_host).pin_memory()
+
+    def bytes_per_group(self, key) -> int:
+        return self.my_bytes
+
+    def bytes_per_step(self) -> int:
+        return self.my_bytes
+
+    def job_bytes(self) -> int:
+        return W.decode_bytes(self.lens_all, self.H, self.HKV, self.D)
+
+    def call_bytes(self, key) -> int:
+        return self.my_bytes
+
+    def calls_per_group(self) -> int:
+        return 1
+
+    def workspace_bytes(self, A) -> int:
+        return A.decode_workspace_size(self.U, self.G, 1, self.D, self.max_len)
+
+    def run_group(self, A, key, stream) -> None:
+        A.decode_attn_batched(self.q, self.kpool, self.vpool, self.offs, self.lens, self.out,
+                              self.U, self.G, 1, self.D, self.rows, self.max_len, stream)
+
+    def run_group_e2e(self, A, key, stream) -> None:
+        self.q.copy_(self.q_host, non_blocking=True)
+        self.run_group(A, key, stream)
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    def e2e_bytes(self):
+        n = self.U * self.G * self.D * 2
+        return n, n
+
+    def config(self):
+        return {
+            "workload": "cfg3: Qwen2-7B-shape batched decode attention, 64 sequences, ragged "
+                        "kv_len U{1024..8192} (seed 2), sharded by (sequence, kv head)",
+            "model": "Qwen2-7B attention shape (random data)",
+            "global_batch": 64, "num_heads": self.H, "num_kv_heads": self.HKV,
+            "head_dim": self.D, "total_kv_tokens": int(self.lens_all.sum()),
+            "units_this_rank": self.U,
+            "l2": "flushed (256 MiB write) before each call; events exclude the flush",
+        }
+
+
+class Cfg4:
+    """Qwen2-7B long context: one sequence, kv_len 131072, H28 Hkv4 D128.
+    One GPU: a plain fr_decode_attn call.  N GPUs: each rank holds a
+    contiguous KV range, computes its (m, l, acc) states, one NCCL all-gather
+    exchanges them and every rank merges.  Total work is fixed ("strong")."""
+
+    H, HKV, D, T = 28, 4, 128, 131072
+    scaling = "strong"
+
+    def __init__(self, torch, rank: int, world: int, device):
+        from forgert_b200 import sharding as SH
+        self.torch = torch
+        self.world = world
+        b, e = SH.kv_ranges(self.T, world)[rank]
+        self.n = e - b
+        g = torch.Generator(device=device)
+        g.manual_seed(3 + 1000 * rank)
+        self.k = torch.empty((max(self.n, 1), self.HKV, self.D), dtype=torch.float16,
+                             device=device).normal_(generator=g)
+        self.v = torch.empty_like(self.k).normal_(generator=g)
+        self.q = torch.empty((self.H, self.D), dtype=torch.float16, device=device)
+        self.q.normal_(generator=torch.Generator(device=device).manual_seed(33))
+        self.out = torch.empty_like(self.q)
+        self.groups = ["step"]
+        self.dec = SH.LongContextDecoder(self.H, self.HKV, self.D, device) if world > 1 else None
+        self.graphable = world == 1
+        self.my_bytes = W.decode_bytes([self.n], self.H, self.HKV, self.D)
+        self.q_host = self.q.cpu().pin_memory()
+        self.out_host = torch.empty_like(self.q_host).pin_memory()
+
+    def bytes_per_group(self, key) -> int:
+        return self.my_bytes
+
+    def bytes_per_step(self) -> int:
+        return self.my_bytes
+
+    def job_bytes(self) -> int:
+        return W.decode_bytes([self.T], self.H, self.HKV, self.D)
+
+    def call_bytes(self, key) -> int:
+        return self.my_bytes
+
+    def calls_per_group(self) -> int:
+        return 1
+
+    def workspace_bytes(self, A) -> int:
+        return A.decode_workspace_size(1, self.H, self.HKV, self.D, max(self.n, 1))
+
+    def run_group(self, A, key, stream) -> None:
+        if self.dec is None:
+            A.decode_attn_v4_flash(self.q, self.k, self.v, self.out, self.H, self.HKV, self.D,
+                                   self.n, stream)
+        else:
+            self.dec(self.q, self.k, self.v, self.n, self.out, stream)
+
+    def run_group_e2e(self, A, key, stream) -> None:
+        self.q.copy_(self.q_host, non_blocking=True)
+        self.run_group(A, key, stream)
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    def e2e_bytes(self):
+        n = self.H * self.D * 2
+        return n, n
+
+    def config(self):
+        return {
+            "workload": "cfg4: Qwen2-7B-shape long-context decode attention, 1 sequence, "
+                        "kv_len 131072, KV range split across GPUs + NCCL all-gather of "
+                        "(m, l, acc) + LSE merge",
+            "model": "Qwen2-7B attention shape (random data)",
+            "global_batch": 1, "num_heads": self.H, "num_kv_heads": self.HKV,
+            "head_dim": self.D, "kv_len": self.T, "kv_rows_this_rank": self.n,
+            "l2": "flushed (256 MiB write) before each step; events exclude the flush",
+        }
+
+
 def run_ours(args, torch, dist, rank, local_rank, world):
     from forgert_b200 import attention as A
     from forgert_b200 import _lib
@@ -241,9 +402,12 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     lib = _lib.load()
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    if args.workload != "cfg2":
-        raise SystemExit(f"workload {args.workload} not implemented yet")
-    wl = Cfg2(torch, rank, device)
+    if args.workload == "cfg2":
+        wl = Cfg2(torch, rank, device)
+    elif args.workload == "cfg3":
+        wl = Cfg3(torch, rank, world, device)
+    else:
+        wl = Cfg4(torch, rank, world, device)
     stream = torch.cuda.Stream(device)
     # Decode-step launch overlap: the attention kernel may stream K/V rows
     # older than the newest one while the preceding kernel finishes.
@@ -258,7 +422,7 @@ def run_ours(args, torch, dist, rank, local_rank, world):
             wl.run_group(A, kv, stream)
     torch.cuda.synchronize()
 
-    use_graph = not args.no_graph
+    use_graph = not args.no_graph and wl.graphable
     graphs = {}
     launches_per_step = 0
     if use_graph:
@@ -321,8 +485,8 @@ def run_ours(args, torch, dist, rank, local_rank, world):
         t = torch.tensor([total_ms], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         max_ms = float(t.item())
-    total_bytes = wl.bytes_per_step() * K * world
-    value = total_bytes / (max_ms * 1e-3) / 1e9
+    job_bytes = wl.job_bytes() if hasattr(wl, "job_bytes") else wl.bytes_per_step() * world
+    value = job_bytes * K / (max_ms * 1e-3) / 1e9
 
     # ---- end to end through the C ABI with pinned host buffers (eager calls)
     e2e = None
@@ -351,7 +515,7 @@ def run_ours(args, torch, dist, rank, local_rank, world):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = float(t.item())
         h2d, d2h = wl.e2e_bytes()
-        e2e = {"value": wl.bytes_per_step() * Ke * world / (e_ms * 1e-3) / 1e9, "unit": UNIT,
+        e2e = {"value": job_bytes * Ke / (e_ms * 1e-3) / 1e9, "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "how": "per call: H2D q from pinned host, fr_decode_attn, D2H out to pinned host; "
                       "eager launches, CUDA events, L2 flushed per kv_len group"}
@@ -362,31 +526,34 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     sweep = {}
     for kv in wl.groups:
         us = group_ms[kv] * 1e3 / (K * wl.calls_per_group())
-        gbs = W.decode_bytes([kv], wl.H, wl.HKV, wl.D) / (us * 1e-6) / 1e9
+        gbs = wl.call_bytes(kv) / (us * 1e-6) / 1e9
         sweep[str(kv)] = {"us_per_call": round(us, 3), "gbs": round(gbs, 1),
                           "frac_of_measured_hbm": round(gbs / peak, 4)}
-    dom = str(max(wl.groups))
-    tr = traffic_per_launch()
+    dom = str(wl.groups[-1])
+    tr = traffic_per_launch() if args.workload == "cfg2" else None
     roofline = {
         "bound": "hbm",
         "kernel": f"split_decode_kernel (one fr_decode_attn call, merge fused), kv_len {dom}",
         "achieved": sweep[dom]["gbs"], "peak": peak, "unit": "GB/s",
         "frac": round(sweep[dom]["gbs"] / peak, 4), "peak_kind": peak_kind,
         "traffic": tr.get("dram_bytes_per_launch") if tr else None,
-        "algorithmic_bytes_per_launch": W.decode_bytes([int(dom)], wl.H, wl.HKV, wl.D),
+        "algorithmic_bytes_per_launch": wl.call_bytes(wl.groups[-1]),
     }
     cfg = wl.config()
-    cfg.update({"parallelism": f"dp{world} (one sequence per GPU)", "graph": use_graph,
+    par = {"cfg2": f"dp{world} (one sequence per GPU)",
+           "cfg3": f"{world} GPUs, (sequence, kv head) units by LPT, no collective",
+           "cfg4": f"{world} GPUs, KV range split, all-gather of states"}[args.workload]
+    cfg.update({"parallelism": par, "graph": use_graph,
                 "launch_overlap": not args.no_overlap, "sweep": sweep})
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(max_ms / K, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+        "scaling": wl.scaling, "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
         "data": "synthetic N(0,1) fp16", "config": cfg, "roofline": roofline,
         "gpu_launches": int(launches_per_step * K), "e2e": e2e,
         "clocks": sampler.summary() if sampler else None,
     }
-    if world == 1 and not args.no_cpu_baseline and not args.ncu:
+    if world == 1 and not args.no_cpu_baseline and not args.ncu and args.workload == "cfg2":
         line["cpu_baseline"] = cpu_baseline_cfg2(budget_s=12.0)
     emit(line)
 

@@ -26,9 +26,9 @@ namespace {
 using fr::DecodeParams;
 
 constexpr int kVersion = 100;     // 0.1.0
-constexpr int kTile = 64;         // KV positions per pipeline stage
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = 32 * (kConsumerWarps + 1);
+constexpr int kConsumerWarps = 4;       // each takes 16 positions of a pipeline stage
+constexpr int kTile = 16 * kConsumerWarps;
+inline int tile_rows() { return kTile; }
 
 constexpr int kClusterCtas = 8;         // cluster size of the fused merge
 constexpr int kMaxUnits = 1 << 16;      // fused-merge counters kept per device
@@ -105,6 +105,8 @@ int ensure_workspace(DeviceState* st, size_t bytes, cudaStream_t s) {
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+int env_int(const char* name, int dflt);
+
 // ------------------------------------------------------------ tensor maps
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
@@ -120,10 +122,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // View of a cache [rows][Hkv][D] fp16 as a 4-D tensor [rows][Hkv][D/64][64]
-// (innermost first below), box = 64 dims x kTile rows of one kv head,
+// (innermost first below), box = 64 dims x tile_rows() rows of one kv head,
 // 128-byte swizzle.  Rows >= `rows` read as zeros.
 int encode_kv_map(CUtensorMap* map, const void* base, int head_dim, int num_kv_heads,
                   long long rows) {
+    const int kTile = tile_rows();
     std::memset(map, 0, sizeof(*map));
     if (rows <= 0) return FR_OK;                      // never read (empty range)
     if (rows > (1LL << 31)) return FR_ERR_INVALID_ARG;
@@ -135,16 +138,19 @@ int encode_kv_map(CUtensorMap* map, const void* base, int head_dim, int num_kv_h
                                    (cuuint64_t)num_kv_heads * head_dim * 2};
     const cuuint32_t box[4] = {64, 1, 1, (cuuint32_t)kTile};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
+    static const int promo = env_int("FORGERT_L2_PROMO", 3);
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides,
                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    static_cast<CUtensorMapL2promotion>(promo & 3),
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return cuda_fail(cudaErrorInvalidValue);
     return FR_OK;
 }
 
 // ------------------------------------------------------------- kernel table
-// One instantiation per (head_dim, head tile).  The stage count keeps 48 KB
-// (D=64, 6 stages) / 96 KB (D=128, 3 stages) of K/V in flight per CTA.
+// One instantiation per (head_dim, head tile, cluster size).  Stages of
+// 16 KB (D=64) / 32 KB (D=128) K+V; the ring keeps 96 KB in flight per CTA,
+// so two CTAs fit on an SM.
 template <int D> struct Stages;
 template <> struct Stages<64> { static constexpr int value = 6; };
 template <> struct Stages<128> { static constexpr int value = 3; };
@@ -158,21 +164,28 @@ auto kernel_ptr() {
 }
 
 template <int D, int NT>
+using SmemOf = fr::SplitSmem<D, NT, kTile, Stages<D>::value, kConsumerWarps>;
+
+template <int D, int NT, int CL>
+int set_smem_attr() {
+    cudaError_t e = cudaFuncSetAttribute(kernel_ptr<D, NT, CL>(),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(SmemOf<D, NT>::kBytes));
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
+
+template <int D, int NT>
 int prepare_kernel(DeviceState* st) {
-    using Smem = fr::SplitSmem<D, NT, kTile, Stages<D>::value, kConsumerWarps>;
     constexpr int slot = kernel_slot<D, NT>();
     if (!(st->attr_done & (1u << slot))) {
-        cudaError_t e = cudaFuncSetAttribute(kernel_ptr<D, NT, 1>(),
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(Smem::kBytes));
-        if (e != cudaSuccess) return cuda_fail(e);
-        e = cudaFuncSetAttribute(kernel_ptr<D, NT, kClusterCtas>(),
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(Smem::kBytes));
-        if (e != cudaSuccess) return cuda_fail(e);
+        int rc = set_smem_attr<D, NT, 1>();
+        if (rc == FR_OK) rc = set_smem_attr<D, NT, 2>();
+        if (rc == FR_OK) rc = set_smem_attr<D, NT, 4>();
+        if (rc == FR_OK) rc = set_smem_attr<D, NT, 8>();
+        if (rc != FR_OK) return rc;
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel_ptr<D, NT, 1>(), kThreads,
-                                                          Smem::kBytes);
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &n, kernel_ptr<D, NT, 1>(), 32 * (kConsumerWarps + 1), SmemOf<D, NT>::kBytes);
         st->occupancy[slot] = (e == cudaSuccess && n > 0) ? n : 1;
         st->attr_done |= (1u << slot);
     }
@@ -182,18 +195,17 @@ int prepare_kernel(DeviceState* st) {
 // Launch with optional cluster shape and programmatic dependent launch.
 template <int D, int NT, int CL>
 int launch_split(const DecodeParams& p, dim3 grid, cudaStream_t s, bool pdl) {
-    using Smem = fr::SplitSmem<D, NT, kTile, Stages<D>::value, kConsumerWarps>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = Smem::kBytes;
+    cfg.blockDim = dim3(32 * (kConsumerWarps + 1), 1, 1);
+    cfg.dynamicSmemBytes = SmemOf<D, NT>::kBytes;
     cfg.stream = s;
     cudaLaunchAttribute attrs[2];
     unsigned n = 0;
     if (CL > 1) {
         attrs[n].id = cudaLaunchAttributeClusterDimension;
-        attrs[n].val.clusterDim.x = CL;
-        attrs[n].val.clusterDim.y = 1;
+        attrs[n].val.clusterDim.x = 1;
+        attrs[n].val.clusterDim.y = CL;
         attrs[n].val.clusterDim.z = 1;
         ++n;
     }
@@ -211,25 +223,34 @@ int launch_split(const DecodeParams& p, dim3 grid, cudaStream_t s, bool pdl) {
     return FR_OK;
 }
 
+template <int D, int NT>
+int launch_split_nt(const DecodeParams& p, int cl, dim3 grid, cudaStream_t s, bool pdl) {
+    switch (cl) {
+        case 8: return launch_split<D, NT, 8>(p, grid, s, pdl);
+        case 4: return launch_split<D, NT, 4>(p, grid, s, pdl);
+        case 2: return launch_split<D, NT, 2>(p, grid, s, pdl);
+        default: return launch_split<D, NT, 1>(p, grid, s, pdl);
+    }
+}
+
 template <int D>
 int launch_split_any(const DecodeParams& p, int nt, int cl, dim3 grid, cudaStream_t s, bool pdl) {
-    if (cl > 1)
-        return nt == 1 ? launch_split<D, 1, kClusterCtas>(p, grid, s, pdl)
-                       : launch_split<D, 2, kClusterCtas>(p, grid, s, pdl);
-    return nt == 1 ? launch_split<D, 1, 1>(p, grid, s, pdl) : launch_split<D, 2, 1>(p, grid, s, pdl);
+    return nt == 1 ? launch_split_nt<D, 1>(p, cl, grid, s, pdl)
+                   : launch_split_nt<D, 2>(p, cl, grid, s, pdl);
 }
 
 struct Plan {
     int nt = 1;            // 8-head tiles per CTA (1 or 2)
     int head_groups = 1;   // CTAs per kv head along the query group
     int num_splits = 1;
-    int split_len = 0;     // positions per split, multiple of kTile
+    int split_len = 0;     // positions per split, multiple of tile_rows()
 };
 
 // Splits the longest sequence so the grid fills the GPU about `waves` times:
 // units = batch * kv_heads * head_groups CTAs per split.
 Plan make_plan(int sm_count, int occ, int batch, int num_kv_heads, int group, int max_kv_len,
                int waves) {
+    const int kTile = tile_rows();
     Plan pl;
     pl.nt = group <= 8 ? 1 : 2;
     pl.head_groups = (group + 8 * pl.nt - 1) / (8 * pl.nt);
@@ -277,31 +298,51 @@ int check_heads(int num_heads, int num_kv_heads, int head_dim) {
 
 // Tuning knobs (read once): FORGERT_SLOTS_PER_SM caps the CTAs per SM the
 // planner fills (default: the occupancy limit); FORGERT_CLUSTER_MIN_SPLITS is
-// the split count from which the fused merge uses clusters (default 2, 0 =
+// the split count from which the fused merge uses clusters (default 8, 0 =
 // never).
 int env_int(const char* name, int dflt) {
     const char* v = std::getenv(name);
     return (v && *v) ? std::atoi(v) : dflt;
 }
 
-int slots_per_sm(int occ) {
+// Single-sequence calls (waves == 1) plan one CTA per SM: with the other
+// slot free, the next call's CTAs can become resident and start streaming
+// K/V while this call merges (programmatic dependent launch).
+int slots_per_sm(int occ, int waves) {
     static const int cap = env_int("FORGERT_SLOTS_PER_SM", 0);
-    return cap > 0 ? std::min(cap, occ) : occ;
+    if (cap > 0) return std::min(cap, occ);
+    return waves == 1 ? 1 : occ;
+}
+
+
+int max_splits() {
+    static const int v = env_int("FORGERT_MAX_SPLITS", 0);
+    return v;
 }
 
 int cluster_min_splits() {
-    static const int v = env_int("FORGERT_CLUSTER_MIN_SPLITS", 2);
+    static const int v = env_int("FORGERT_CLUSTER_MIN_SPLITS", kClusterCtas);
     return v;
 }
 
 int plan_for(DeviceState* st, int head_dim, int batch, int num_kv_heads, int group,
              int max_kv_len, int waves, Plan* pl) {
     const int nt = group <= 8 ? 1 : 2;
-    int rc = head_dim == 64 ? (nt == 1 ? prepare_kernel<64, 1>(st) : prepare_kernel<64, 2>(st))
-                            : (nt == 1 ? prepare_kernel<128, 1>(st) : prepare_kernel<128, 2>(st));
+    const int kTile = tile_rows();
+    int rc;
+    rc = head_dim == 64 ? (nt == 1 ? prepare_kernel<64, 1>(st) : prepare_kernel<64, 2>(st))
+                        : (nt == 1 ? prepare_kernel<128, 1>(st) : prepare_kernel<128, 2>(st));
     if (rc != FR_OK) return rc;
-    const int occ = slots_per_sm(st->occupancy[head_dim == 64 ? (nt - 1) : (2 + nt - 1)]);
+    const int slot = (head_dim == 64 ? 0 : 2) + (nt - 1);
+    const int occ = slots_per_sm(st->occupancy[slot], waves);
     *pl = make_plan(st->sm_count, occ, batch, num_kv_heads, group, max_kv_len, waves);
+    const int cap = max_splits();
+    if (cap > 0 && pl->num_splits > cap) {
+        const int tiles = std::max(1, (max_kv_len + kTile - 1) / kTile);
+        const int tps = (tiles + cap - 1) / cap;
+        pl->split_len = tps * kTile;
+        pl->num_splits = (tiles + tps - 1) / tps;
+    }
     return FR_OK;
 }
 
@@ -324,16 +365,34 @@ int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* 
     rc = plan_for(st, D, batch, p.Hkv, group, max_kv_len, waves, &pl);
     if (rc != FR_OK) return rc;
     const long long units = (long long)batch * p.Hkv * pl.head_groups;
+    // Cluster size: the largest of 8/4/2 whose whole clusters cover nearly as
+    // many splits as the plan wants (every SM busy matters more than the
+    // merge depth); fewer than cluster_min_splits() splits merge without
+    // clusters (batched calls hide that merge behind other units).
     const int cmin = cluster_min_splits();
-    const int cl = (cmin > 0 && pl.num_splits >= cmin) ? kClusterCtas : 1;
+    int cl = 1;
+    if (cmin > 0 && pl.num_splits >= cmin) {
+        const int want = pl.num_splits;
+        cl = 8;
+        for (int c : {4, 2})
+            if ((want / c) * c * 20 >= (want / cl) * cl * 21) cl = c;   // > 5% more splits
+        const int kTile = tile_rows();
+        const int tiles = std::max(1, (max_kv_len + kTile - 1) / kTile);
+        const int nsp = std::max(cl, want / cl * cl);
+        const int tps = (tiles + nsp - 1) / nsp;
+        pl.split_len = tps * kTile;
+        pl.num_splits = (tiles + tps - 1) / tps;
+    }
     const bool fused = units * cl <= kMaxUnits;      // one counter per (unit, cluster rank)
-    const int splits = (pl.num_splits + cl - 1) / cl * cl;     // padded splits are empty
+    const int splits = (pl.num_splits + cl - 1) / cl * cl;     // pads at most one cluster
     p.G = group;
     p.split_len = pl.split_len;
     p.num_splits = splits;
     p.head_groups = pl.head_groups;
     p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
     p.err = st->err;
+    static const int evict_normal = env_int("FORGERT_EVICT_NORMAL", 0);
+    p.evict_normal = evict_normal;
     const bool pdl = s != nullptr;
     const long long rows = (long long)batch * p.H;
     if (final_out && splits == 1) {
@@ -353,7 +412,7 @@ int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* 
             p.out_acc = state_acc;
         }
     }
-    dim3 grid(splits, p.Hkv * pl.head_groups, batch);
+    dim3 grid(p.Hkv * pl.head_groups, splits, batch);
     rc = D == 64 ? launch_split_any<64>(p, pl.nt, cl, grid, s, pdl)
                  : launch_split_any<128>(p, pl.nt, cl, grid, s, pdl);
     if (rc != FR_OK || p.write_final || p.counters) return rc;
@@ -699,7 +758,7 @@ extern "C" int fr_decode_attn_noalloc(const void* q, const void* k_cache, const 
         p.part_acc = nd->scratch + (size_t)num_heads * pl.num_splits * 2;
     }
     p.part_slots = pl.num_splits;
-    dim3 grid(pl.num_splits, p.Hkv * pl.head_groups, 1);
+    dim3 grid(p.Hkv * pl.head_groups, pl.num_splits, 1);
     rc = head_dim == 64 ? launch_split_any<64>(p, pl.nt, 1, grid, s, false)
                         : launch_split_any<128>(p, pl.nt, 1, grid, s, false);
     if (rc != FR_OK || direct) return rc;

@@ -60,8 +60,8 @@ struct DecodeParams {
                                  // kernels); 0 = everything waits
     int H, Hkv, G;               // query heads, kv heads, group size H / Hkv
     int split_len;               // positions per split (multiple of TILE)
-    int num_splits;              // gridDim.x
-    int head_groups;             // gridDim.y / Hkv
+    int num_splits;              // gridDim.y
+    int head_groups;             // gridDim.x / Hkv
     float scale_log2;            // log2(e) / sqrt(D)
     int write_final;             // 1: single split, write normalised fp16 to out
     __half* out;                 // [B, H, D]
@@ -73,6 +73,7 @@ struct DecodeParams {
     int* counters;               // fused merge: one per (b, kv head, head group), zero
                                  // between calls; nullptr = unfused (lse_merge_kernel follows)
     int* err;                    // device error word
+    int evict_normal;            // 1: K/V loads without the L2 evict-first hint
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {
@@ -126,7 +127,7 @@ __device__ __forceinline__ uint32_t swz_offset(int r, int col) {
 
 // ---------------------------------------------------------------------------
 // Split-KV decode kernel.
-//   grid  = (num_splits, Hkv * head_groups, B), clusters of CL CTAs along x
+//   grid  = (Hkv * head_groups, num_splits, B), clusters of CL CTAs along y
 //   block = 32 * (NW + 1): NW consumer warps + 1 producer warp
 //
 // Output paths (chosen by the host, uniform over the grid):
@@ -171,9 +172,11 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int split = blockIdx.x;
-    const int kvh = blockIdx.y / p.head_groups;
-    const int hgrp = blockIdx.y % p.head_groups;
+    // x = (kv head, head group): the CTAs that read the same cache rows of
+    // one split launch back to back and stream those rows together.
+    const int split = blockIdx.y;
+    const int kvh = blockIdx.x / p.head_groups;
+    const int hgrp = blockIdx.x % p.head_groups;
     const int b = blockIdx.z;
 
     // Heads served by this CTA: h0 .. h0 + gcount - 1.
@@ -210,7 +213,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         if (lane == 0 && ntiles > 0) {
             prefetch_tensormap(&p.kmap);
             prefetch_tensormap(&p.vmap);
-            const uint64_t policy = l2_policy_evict_first();
+            const uint64_t policy = p.evict_normal ? l2_policy_evict_normal() : l2_policy_evict_first();
             bool waited = false;
             int issued = 0;
             for (int i = 0; i < ntiles; ++i) {

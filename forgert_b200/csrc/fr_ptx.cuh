@@ -60,13 +60,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                  :: "r"(smem_u32(bar)) : "memory");
 }
 
+// The waiting thread is suspended until the phase completes or, at the
+// latest, after kSuspendHintNs, so idle warps do not spin on issue slots the
+// computing warps need.
+constexpr uint32_t kSuspendHintNs = 20000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs) : "memory");
     return ok != 0;
 }
 
@@ -122,6 +127,12 @@ __device__ __forceinline__ void bulk_g2s_evict_first(void* dst_smem, const void*
         "[%0], [%1], %2, [%3], %4;"
         :: "r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
 }
 
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {

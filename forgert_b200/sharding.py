@@ -113,18 +113,19 @@ class LongContextDecoder:
     def views(self, buf):
         return buf[:2 * self.H].view(self.H, 2), buf[2 * self.H:].view(self.H, self.D)
 
-    def _cuda_partial(self, q, k_local, v_local, local_len, state_ml, state_acc):
+    def _cuda_partial(self, q, k_local, v_local, local_len, state_ml, state_acc, stream=None):
         from . import attention as A
         A.decode_attn_partial(q, k_local if local_len else 0, v_local if local_len else 0,
-                              local_len, state_ml, state_acc, self.H, self.Hkv, self.D)
+                              local_len, state_ml, state_acc, self.H, self.Hkv, self.D, stream)
 
-    def _cuda_merge(self, gathered, world, out):
+    def _cuda_merge(self, gathered, world, out, stream=None):
         from ._lib import check, load
+        from .attention import _stream
         lib = load()
         base = gathered.data_ptr()
         check("fr_lse_merge_strided", lib.fr_lse_merge_strided(
             base, base + 2 * self.H * 4, world, out.data_ptr(), self.H, self.D,
-            self.state_elems, self.state_elems, None))
+            self.state_elems, self.state_elems, _stream(stream)))
 
     def exchange(self) -> None:
         if self.world == 1:
@@ -134,8 +135,15 @@ class LongContextDecoder:
         else:
             self.dist.all_gather(list(self.gathered.unbind(0)), self.local, group=self.group)
 
-    def __call__(self, q, k_local, v_local, local_len: int, out) -> None:
+    def __call__(self, q, k_local, v_local, local_len: int, out, stream=None) -> None:
+        """One decode step.  `stream` (CUDA path) must be the current torch
+        stream, on which the all-gather is issued."""
         ml, acc = self.views(self.local)
-        self.partial_fn(q, k_local, v_local, local_len, ml, acc)
-        self.exchange()
-        self.merge_fn(self.gathered, self.world, out)
+        if stream is None:
+            self.partial_fn(q, k_local, v_local, local_len, ml, acc)
+            self.exchange()
+            self.merge_fn(self.gathered, self.world, out)
+        else:
+            self.partial_fn(q, k_local, v_local, local_len, ml, acc, stream)
+            self.exchange()
+            self.merge_fn(self.gathered, self.world, out, stream)
