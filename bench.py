@@ -344,7 +344,10 @@ class Cfg4:
         self.out = torch.empty_like(self.q)
         self.groups = ["step"]
         self.dec = SH.LongContextDecoder(self.H, self.HKV, self.D, device) if world > 1 else None
-        self.graphable = world == 1
+        # N > 1: the NCCL all-gather is captured in the same CUDA graph as the
+        # partial and merge kernels (graphs are released before the process
+        # group is destroyed).
+        self.graphable = True
         self.my_bytes = W.decode_bytes([self.n], self.H, self.HKV, self.D)
         self.q_host = self.q.cpu().pin_memory()
         self.out_host = torch.empty_like(self.q_host).pin_memory()
@@ -683,6 +686,9 @@ def main():
         run_ours(args, torch, dist, rank, local_rank, world)
     finally:
         if world > 1:
+            import gc
+            gc.collect()                 # CUDA graphs holding NCCL work go first
+            torch.cuda.synchronize()
             dist.destroy_process_group()
 
 

@@ -11,7 +11,7 @@
 //
 // Data movement: warp NW (the producer) streams K and V tiles of TILE
 // positions x 64 head dims into shared memory with 4-D TMA tensor copies
-// (cp.async.bulk.tensor, no multicast): the tensor map views a cache as
+// (cp.async.bulk.tensor, each load into this CTA only): the tensor map views a cache as
 // [rows][kv_heads][D/64][64] fp16, one box = 64 dims x TILE rows of one kv
 // head, written with the 128-byte swizzle (16-byte chunk c of row r lands at
 // chunk c ^ (r & 7)), which makes the ldmatrix reads below conflict-free.

@@ -3,7 +3,7 @@
 // Thin inline-PTX wrappers for the Blackwell data-movement and tensor paths
 // the kernels are built on:
 //   * mbarrier phase tracking with expect-tx accounting (bounded waits),
-//   * cp.async.bulk (TMA bulk copy, global -> shared, no multicast),
+//   * cp.async.bulk / cp.async.bulk.tensor (TMA, global -> this CTA's shared memory),
 //   * ldmatrix / movmatrix / mma.sync m16n8k16 (f16 in, f32 accumulate),
 //   * ex2.approx for the base-2 online softmax.
 // Every wait has a time limit: a wait that runs out records an error code in
@@ -86,7 +86,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
-// ------------------------------------------------ TMA tensor copy (no multicast)
+// ------------------------------------------ TMA tensor copy (into this CTA only)
 // 4-D tiled load described by a CUtensorMap that lives in kernel parameter
 // space (__grid_constant__).  Coordinates are element indices, innermost
 // first; out-of-bounds box elements are written as zeros and still count
@@ -105,7 +105,7 @@ __device__ __forceinline__ void prefetch_tensormap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
 }
 
-// ------------------------------------------------- TMA bulk copy (no multicast)
+// ------------------------------------------- TMA bulk copy (into this CTA only)
 // Copies `bytes` (multiple of 16, both addresses 16-byte aligned) from global
 // to this CTA's shared memory and signals completion on `bar` as tx bytes.
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem,
