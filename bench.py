@@ -2,7 +2,7 @@
 """Decode-attention benchmark (one JSON line on rank 0).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload cfg2|cfg3|cfg4]
+                  [--workload cfg2|cfg3|cfg3p|cfg4]
 
 Default workload (cfg2, the configuration the headline metric is quoted on):
 Qwen2-1.5B-shaped decode attention, batch 1, 12 query heads, 2 KV heads,
@@ -23,6 +23,8 @@ data path; value = all ranks' bytes / the slowest rank's time ("weak").
 (sequence, kv head) across ranks, "strong") and cfg4 (one 128K-token
 sequence, KV range split across ranks, NCCL all-gather of the per-rank
 (m, l, acc) states + LSE merge, "strong") measure the multi-GPU paths.
+--workload cfg3p is cfg3 in a paged KV cache (16-row pages in shuffled order,
+one block table per sequence, fr_decode_attn_paged), sharded by sequence.
 
 --impl reference times the reference's own CPU implementation
 (cpu_decode_attn, tests/test_kernels.cpp:229-270, compiled from the
@@ -61,7 +63,10 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference", "refgpu"], default="ours",
                     help="reference = the reference's CPU implementation; refgpu = the "
                          "reference's own v4 GPU kernel built for sm_100a (oracle/_ref)")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg3p", "cfg4"], default="cfg2")
+    ap.add_argument("--page-size", type=int, default=16, help="cfg3p page rows (multiple of 16)")
+    ap.add_argument("--page-order", choices=["shuffled", "sequential"], default="shuffled",
+                    help="cfg3p: pages handed out in a seeded random order, or in order")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of graphs")
     ap.add_argument("--no-overlap", action="store_true",
                     help="disable launch overlap (pre-wait K/V prefetch under PDL)")
@@ -321,6 +326,72 @@ class Cfg3:
         }
 
 
+class Cfg3Paged(Cfg3):
+    """cfg3's 64 sequences in a paged KV cache: pages of page_size rows x 4 kv heads
+    x 128, handed out in a seeded random order (a fragmented serving cache),
+    one block table per sequence, one fr_decode_attn_paged call.  N GPUs:
+    whole sequences are assigned by LPT on length; no collective."""
+
+    def __init__(self, torch, rank: int, world: int, device, page_size: int = 16,
+                 page_order: str = "shuffled"):
+        from forgert_b200 import sharding as SH
+        self.torch = torch
+        self.PAGE = page_size
+        self.lens_all = W.cfg3_lens()
+        mine = SH.lpt_assign(self.lens_all, world)[rank]
+        lens = [int(self.lens_all[i]) for i in mine]
+        self.B = len(mine)
+        need = [-(-n // self.PAGE) for n in lens]
+        self.num_pages = int(sum(need))
+        width = max(need)
+        self.page_order = page_order
+        order = (np.random.default_rng(5 + rank).permutation(self.num_pages)
+                 if page_order == "shuffled" else np.arange(self.num_pages))
+        table = np.full((self.B, width), -1, np.int32)
+        o = 0
+        for b, n in enumerate(need):
+            table[b, :n] = order[o:o + n]
+            o += n
+        g = torch.Generator(device=device)
+        g.manual_seed(2 + 1000 * rank)
+        shape = (self.num_pages, self.PAGE, self.HKV, self.D)
+        self.kpages = torch.empty(shape, dtype=torch.float16, device=device).normal_(generator=g)
+        self.vpages = torch.empty(shape, dtype=torch.float16, device=device).normal_(generator=g)
+        self.table = torch.from_numpy(table).to(device)
+        self.width = width
+        self.lens = torch.tensor(lens, dtype=torch.int32, device=device)
+        self.q = torch.empty((self.B, self.H, self.D), dtype=torch.float16, device=device).normal_(generator=g)
+        self.out = torch.empty_like(self.q)
+        self.max_len = int(max(lens))
+        self.groups = ["batch"]
+        self.my_bytes = W.decode_bytes(lens, self.H, self.HKV, self.D)
+        self.q_host = self.q.cpu().pin_memory()
+        self.out_host = torch.empty_like(self.q_host).pin_memory()
+        self.U = self.B
+
+    def workspace_bytes(self, A) -> int:
+        return A.decode_workspace_size(self.B, self.H, self.HKV, self.D, self.max_len)
+
+    def run_group(self, A, key, stream) -> None:
+        A.decode_attn_paged(self.q, self.kpages, self.vpages, self.table, self.lens, self.out,
+                            self.B, self.H, self.HKV, self.D, self.PAGE, self.num_pages,
+                            self.width, self.max_len, stream)
+
+    def e2e_bytes(self):
+        n = self.B * self.H * self.D * 2
+        return n, n
+
+    def config(self):
+        c = super().config()
+        c["workload"] = (f"cfg3p: cfg3's 64 sequences in a paged KV cache ({self.PAGE}-row pages in "
+                         f"{self.page_order} order, block table per sequence), sharded by sequence")
+        c.pop("units_this_rank", None)
+        c.update({"page_size": self.PAGE, "page_order": self.page_order,
+                  "sequences_this_rank": self.B,
+                  "num_pages_this_rank": self.num_pages})
+        return c
+
+
 class Cfg4:
     """Qwen2-7B long context: one sequence, kv_len 131072, H28 Hkv4 D128.
     One GPU: a plain fr_decode_attn call.  N GPUs: each rank holds a
@@ -411,6 +482,8 @@ def run_ours(args, torch, dist, rank, local_rank, world):
         wl = Cfg2(torch, rank, device)
     elif args.workload == "cfg3":
         wl = Cfg3(torch, rank, world, device)
+    elif args.workload == "cfg3p":
+        wl = Cfg3Paged(torch, rank, world, device, args.page_size, args.page_order)
     else:
         wl = Cfg4(torch, rank, world, device)
     stream = torch.cuda.Stream(device)
@@ -547,6 +620,7 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     cfg = wl.config()
     par = {"cfg2": f"dp{world} (one sequence per GPU)",
            "cfg3": f"{world} GPUs, (sequence, kv head) units by LPT, no collective",
+           "cfg3p": f"{world} GPUs, sequences by LPT, no collective",
            "cfg4": f"{world} GPUs, KV range split, all-gather of states"}[args.workload]
     cfg.update({"parallelism": par, "graph": use_graph,
                 "launch_overlap": not args.no_overlap, "sweep": sweep})

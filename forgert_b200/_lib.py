@@ -29,6 +29,8 @@ SIGNATURES = {
     "fr_decode_attn_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "fr_decode_attn_batched": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i,
                                     ctypes.c_longlong, _i, _vp]),
+    "fr_decode_attn_paged": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i,
+                                  _i, _vp]),
     "fr_decode_attn_partial": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp]),
     "fr_lse_merge": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp]),
     "fr_lse_merge_strided": (_i, [_vp, _vp, _i, _vp, _i, _i, ctypes.c_longlong,

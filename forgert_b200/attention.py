@@ -87,6 +87,20 @@ def decode_attn_batched(q, k_pool, v_pool, row_offsets, kv_lens, out, batch: int
         num_heads, num_kv_heads, head_dim, pool_rows, max_kv_len, _stream(stream)))
 
 
+def decode_attn_paged(q, k_pages, v_pages, block_table, kv_lens, out, batch: int,
+                      num_heads: int, num_kv_heads: int, head_dim: int, page_size: int,
+                      num_pages: int, max_blocks_per_seq: int, max_kv_len: int,
+                      stream=None) -> None:
+    """Batch over a paged cache [num_pages, page_size, Hkv, D]: position t of
+    sequence b is row t % page_size of page block_table[b, t // page_size]
+    (device int32 [batch, max_blocks_per_seq]); kv_lens device int32."""
+    lib = load()
+    check("fr_decode_attn_paged", lib.fr_decode_attn_paged(
+        _ptr(q), _ptr(k_pages), _ptr(v_pages), _ptr(block_table), _ptr(kv_lens), _ptr(out),
+        batch, num_heads, num_kv_heads, head_dim, page_size, num_pages, max_blocks_per_seq,
+        max_kv_len, _stream(stream)))
+
+
 def decode_attn_partial(q, k_cache, v_cache, kv_len: int, state_ml, state_acc, num_heads: int,
                         num_kv_heads: int, head_dim: int, stream=None) -> None:
     """(m, l, acc) log-sum-exp state per head over positions [0, kv_len)."""

@@ -19,6 +19,7 @@
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
+#include <numeric>
 #include <vector>
 
 namespace {
@@ -122,11 +123,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // View of a cache [rows][Hkv][D] fp16 as a 4-D tensor [rows][Hkv][D/64][64]
-// (innermost first below), box = 64 dims x tile_rows() rows of one kv head,
-// 128-byte swizzle.  Rows >= `rows` read as zeros.
+// (innermost first below), box = 64 dims x box_rows (default tile_rows())
+// rows of one kv head, 128-byte swizzle.  Rows >= `rows` read as zeros.
 int encode_kv_map(CUtensorMap* map, const void* base, int head_dim, int num_kv_heads,
-                  long long rows) {
-    const int kTile = tile_rows();
+                  long long rows, int box_rows = 0) {
+    const int kTile = box_rows > 0 ? box_rows : tile_rows();
     std::memset(map, 0, sizeof(*map));
     if (rows <= 0) return FR_OK;                      // never read (empty range)
     if (rows > (1LL << 31)) return FR_ERR_INVALID_ARG;
@@ -158,9 +159,9 @@ template <> struct Stages<128> { static constexpr int value = 3; };
 template <int D, int NT>
 constexpr int kernel_slot() { return (D == 64 ? 0 : 2) + (NT - 1); }
 
-template <int D, int NT, int CL>
+template <int D, int NT, int CL, bool PAGED = false>
 auto kernel_ptr() {
-    return fr::split_decode_kernel<D, NT, kTile, Stages<D>::value, kConsumerWarps, CL>;
+    return fr::split_decode_kernel<D, NT, kTile, Stages<D>::value, kConsumerWarps, CL, PAGED>;
 }
 
 template <int D, int NT>
@@ -168,10 +169,12 @@ using SmemOf = fr::SplitSmem<D, NT, kTile, Stages<D>::value, kConsumerWarps>;
 
 template <int D, int NT, int CL>
 int set_smem_attr() {
-    cudaError_t e = cudaFuncSetAttribute(kernel_ptr<D, NT, CL>(),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(SmemOf<D, NT>::kBytes));
-    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+    for (auto fn : {kernel_ptr<D, NT, CL, false>(), kernel_ptr<D, NT, CL, true>()}) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(SmemOf<D, NT>::kBytes));
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
+    return FR_OK;
 }
 
 template <int D, int NT>
@@ -193,7 +196,7 @@ int prepare_kernel(DeviceState* st) {
 }
 
 // Launch with optional cluster shape and programmatic dependent launch.
-template <int D, int NT, int CL>
+template <int D, int NT, int CL, bool PAGED>
 int launch_split(const DecodeParams& p, dim3 grid, cudaStream_t s, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
@@ -216,27 +219,31 @@ int launch_split(const DecodeParams& p, dim3 grid, cudaStream_t s, bool pdl) {
     }
     cfg.attrs = attrs;
     cfg.numAttrs = n;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel_ptr<D, NT, CL>(), p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel_ptr<D, NT, CL, PAGED>(), p);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return FR_OK;
 }
 
-template <int D, int NT>
+template <int D, int NT, bool PAGED>
 int launch_split_nt(const DecodeParams& p, int cl, dim3 grid, cudaStream_t s, bool pdl) {
     switch (cl) {
-        case 8: return launch_split<D, NT, 8>(p, grid, s, pdl);
-        case 4: return launch_split<D, NT, 4>(p, grid, s, pdl);
-        case 2: return launch_split<D, NT, 2>(p, grid, s, pdl);
-        default: return launch_split<D, NT, 1>(p, grid, s, pdl);
+        case 8: return launch_split<D, NT, 8, PAGED>(p, grid, s, pdl);
+        case 4: return launch_split<D, NT, 4, PAGED>(p, grid, s, pdl);
+        case 2: return launch_split<D, NT, 2, PAGED>(p, grid, s, pdl);
+        default: return launch_split<D, NT, 1, PAGED>(p, grid, s, pdl);
     }
 }
 
+// The paged instantiation is chosen by p.block_table.
 template <int D>
 int launch_split_any(const DecodeParams& p, int nt, int cl, dim3 grid, cudaStream_t s, bool pdl) {
-    return nt == 1 ? launch_split_nt<D, 1>(p, cl, grid, s, pdl)
-                   : launch_split_nt<D, 2>(p, cl, grid, s, pdl);
+    if (p.block_table)
+        return nt == 1 ? launch_split_nt<D, 1, true>(p, cl, grid, s, pdl)
+                       : launch_split_nt<D, 2, true>(p, cl, grid, s, pdl);
+    return nt == 1 ? launch_split_nt<D, 1, false>(p, cl, grid, s, pdl)
+                   : launch_split_nt<D, 2, false>(p, cl, grid, s, pdl);
 }
 
 struct Plan {
@@ -483,6 +490,37 @@ int fr_decode_attn_batched(const void* q, const void* k_pool, const void* v_pool
     p.kv_lens = kv_lens;
     p.zero_tail = 1;
     // Ragged batches: several waves of shorter splits balance the tail.
+    return run_decode(p, head_dim, batch, std::max(1, max_kv_len), static_cast<__half*>(out),
+                      nullptr, nullptr, 4, static_cast<cudaStream_t>(stream));
+}
+
+int fr_decode_attn_paged(const void* q, const void* k_pages, const void* v_pages,
+                         const int* block_table, const int* kv_lens, void* out, int batch,
+                         int num_heads, int num_kv_heads, int head_dim, int page_size,
+                         int num_pages, int max_blocks_per_seq, int max_kv_len, void* stream) {
+    if (!q || !k_pages || !v_pages || !block_table || !kv_lens || !out || batch <= 0 ||
+        num_pages <= 0 || max_blocks_per_seq <= 0 || max_kv_len < 0 || page_size <= 0 ||
+        page_size % 16 != 0 || (long long)max_blocks_per_seq * page_size < max_kv_len ||
+        (long long)num_pages * page_size >= (1LL << 31))
+        return FR_ERR_INVALID_ARG;
+    int rc = check_heads(num_heads, num_kv_heads, head_dim);
+    if (rc != FR_OK) return rc;
+    if (!aligned(q, 4) || !aligned(out, 4) || !aligned(k_pages, 16) || !aligned(v_pages, 16) ||
+        !aligned(block_table, 4) || !aligned(kv_lens, 4))
+        return FR_ERR_MISALIGNED;
+    DecodeParams p = base_params(q, num_heads, num_kv_heads);
+    const int box = std::gcd(page_size, tile_rows());    // a box never straddles a page
+    const long long rows = (long long)num_pages * page_size;
+    rc = encode_kv_map(&p.kmap, k_pages, head_dim, num_kv_heads, rows, box);
+    if (rc == FR_OK) rc = encode_kv_map(&p.vmap, v_pages, head_dim, num_kv_heads, rows, box);
+    if (rc != FR_OK) return rc;
+    p.block_table = block_table;
+    p.bt_stride = max_blocks_per_seq;
+    p.page_size = page_size;
+    p.page_box = box;
+    p.num_pages = num_pages;
+    p.kv_lens = kv_lens;
+    p.zero_tail = 1;        // the last page's rows past the end may hold anything
     return run_decode(p, head_dim, batch, std::max(1, max_kv_len), static_cast<__half*>(out),
                       nullptr, nullptr, 4, static_cast<cudaStream_t>(stream));
 }

@@ -74,6 +74,15 @@ struct DecodeParams {
                                  // between calls; nullptr = unfused (lse_merge_kernel follows)
     int* err;                    // device error word
     int evict_normal;            // 1: K/V loads without the L2 evict-first hint
+    // Paged KV (kernel instantiated with PAGED): the tensor maps view the page
+    // pool [num_pages * page_size rows][Hkv][D/64][64]; logical position t of
+    // sequence b is row block_table[b * bt_stride + t / page_size] * page_size
+    // + t % page_size.
+    const int* block_table;      // [B, bt_stride] page ids
+    int bt_stride;               // entries per block-table row
+    int page_size;               // rows per page, multiple of 16
+    int page_box;                // rows per TMA box: gcd(page_size, TILE)
+    int num_pages;               // pool size; other ids read as zeros
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {
@@ -147,7 +156,7 @@ __device__ __forceinline__ uint32_t swz_offset(int r, int col) {
 // (griddepcontrol.wait) before it reads q or writes anything; K/V tiles of
 // rows below prefetch_rows may stream in before that wait.
 // ---------------------------------------------------------------------------
-template <int D, int NT, int TILE, int STAGES, int NW, int CL>
+template <int D, int NT, int TILE, int STAGES, int NW, int CL, bool PAGED>
 __global__ void __launch_bounds__(32 * (NW + 1))
 split_decode_kernel(const __grid_constant__ DecodeParams p) {
     static_assert(D % 64 == 0, "head_dim must be a multiple of 64");
@@ -208,7 +217,80 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     float o[DTILES][NT][4];
     float m_run[NT][2], l_run[NT][2];
 
-    if (warp == NW) {
+    if (PAGED && warp == NW) {
+        // -------------------------------------------------- paged producer
+        // The whole warp walks the tiles.  Block-table entries are held 32 per
+        // coalesced load (lane j: entry win + j; the next 32 already in
+        // flight); lane j < TILE / page_box issues the copies of box j of the
+        // tile, so one pass of the warp covers a tile whatever the page size.
+        // Boxes past the end of the sequence, and page ids outside the pool,
+        // read as zeros (a row coordinate past the tensor map).
+        if (ntiles > 0) {
+            if (lane == 0) {
+                prefetch_tensormap(&p.kmap);
+                prefetch_tensormap(&p.vmap);
+            }
+            const uint64_t policy = p.evict_normal ? l2_policy_evict_normal() : l2_policy_evict_first();
+            grid_dependency_wait();                 // the block table may be the preceding grid's output
+            const int* bt = p.block_table + (size_t)b * p.bt_stride;
+            const int nent = min(p.bt_stride, (seq_len + p.page_size - 1) / p.page_size);
+            const int box = p.page_box;
+            const bool boxer = lane < TILE / box;
+            const int oob_row = p.num_pages * p.page_size;
+            int win = pos_begin / p.page_size;
+            int mine = (win + lane < nent) ? __ldg(bt + win + lane) : -1;
+            int ahead = (win + 32 + lane < nent) ? __ldg(bt + win + 32 + lane) : -1;
+            int issued = 0;
+            for (int i = 0; i < ntiles; ++i) {
+                const int s = i % STAGES;
+                if (i >= STAGES) {
+                    const bool w = mbar_wait_bounded(&empty[s], ((i / STAGES) - 1) & 1);
+                    if (!__all_sync(0xffffffffu, w)) {
+                        if (lane == 0) record_error(p.err, kDevTimeoutEmpty);
+                        break;
+                    }
+                }
+                const int t0 = pos_begin + i * TILE;
+                // A tile spans at most TILE / 16 entries, so they lie in
+                // [win, win + 64) once the window has moved past its first one.
+                if (t0 / p.page_size >= win + 32) {
+                    win += 32;
+                    mine = ahead;
+                    ahead = (win + 32 + lane < nent) ? __ldg(bt + win + 32 + lane) : -1;
+                }
+                const int tpos = t0 + lane * box;
+                const int e = tpos / p.page_size;
+                const int k = e - win;
+                const int from_mine = __shfl_sync(0xffffffffu, mine, k & 31);
+                const int from_ahead = __shfl_sync(0xffffffffu, ahead, k & 31);
+                const int page = k < 32 ? from_mine : from_ahead;
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], uint32_t(2 * S::kTileBytes));
+                __syncwarp();
+                if (boxer) {
+                    const int row = (tpos < seq_len && page >= 0 && page < p.num_pages)
+                                        ? page * p.page_size + (tpos - e * p.page_size)
+                                        : oob_row;
+#pragma unroll
+                    for (int sub = 0; sub < S::kSub; ++sub) {
+                        const int o = s * S::kTileBytes + sub * S::kSubBytes + lane * box * 128;
+                        tma_load_4d(kring + o, &p.kmap, 0, sub, kvh, row, &full[s], policy);
+                        tma_load_4d(vring + o, &p.vmap, 0, sub, kvh, row, &full[s], policy);
+                    }
+                }
+                ++issued;
+            }
+            // Drain (as below): no copy may still be in flight at exit.
+            if (lane == 0) {
+                for (int i = max(0, issued - STAGES); i < issued; ++i) {
+                    if (!mbar_wait_bounded(&full[i % STAGES], (i / STAGES) & 1)) {
+                        record_error(p.err, kDevTimeoutFull);
+                        break;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == NW) {
         // -------------------------------------------------------- producer
         if (lane == 0 && ntiles > 0) {
             prefetch_tensormap(&p.kmap);

@@ -96,6 +96,37 @@ def cfg4_inputs(seed: int = 3, kv_len: int = CFG4_SHAPE["kv_len"]):
     return decode_inputs(seed, s["H"], s["Hkv"], s["D"], kv_len)
 
 
+def paginate(ks, vs, page_size: int, seed: int = 7, spare_pages: int = 0, fill=np.nan,
+             table_width: int | None = None):
+    """Lays per-sequence caches ([n_b, Hkv, D] each) out as a paged cache.
+
+    Returns (k_pages, v_pages [num_pages, page_size, Hkv, D], block_table
+    [B, table_width] int32).  Pages are handed out in a seeded random order (a
+    fragmented serving cache); `spare_pages` extra pages are never referenced;
+    unreferenced pages and the rows of each last page past the sequence's end
+    hold `fill`; table entries past a sequence's pages are -1."""
+    Hkv, D = ks[0].shape[1], ks[0].shape[2]
+    need = [-(-int(k.shape[0]) // page_size) for k in ks]
+    width = max(1, max(need)) if table_width is None else table_width
+    num_pages = sum(need) + spare_pages
+    order = np.random.default_rng(seed).permutation(max(num_pages, 1))[:num_pages]
+    k_pages = np.full((max(num_pages, 1), page_size, Hkv, D), fill, np.float16)
+    v_pages = np.full_like(k_pages, fill)
+    table = np.full((len(ks), width), -1, np.int32)
+    nxt = 0
+    for b, (k, v) in enumerate(zip(ks, vs)):
+        n = int(k.shape[0])
+        for j in range(need[b]):
+            pg = int(order[nxt])
+            nxt += 1
+            table[b, j] = pg
+            rows = slice(j * page_size, min(n, (j + 1) * page_size))
+            cnt = rows.stop - rows.start
+            k_pages[pg, :cnt] = k[rows]
+            v_pages[pg, :cnt] = v[rows]
+    return k_pages, v_pages, table
+
+
 def decode_bytes(kv_lens, H: int, Hkv: int, D: int) -> int:
     """Algorithmic bytes of one decode call over a batch with these lengths."""
     lens = np.atleast_1d(np.asarray(kv_lens, dtype=np.int64))

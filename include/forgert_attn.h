@@ -97,6 +97,28 @@ FR_API int fr_decode_attn_batched(const void* q, const void* k_pool, const void*
                                   int batch, int num_heads, int num_kv_heads, int head_dim,
                                   long long pool_rows, int max_kv_len, void* stream);
 
+/* Batched decode over a paged KV cache (block table).
+ *   k_pages, v_pages  [num_pages, page_size, num_kv_heads, head_dim] fp16
+ *                     (16-byte aligned): each page holds page_size cache rows
+ *                     in the reference's row layout
+ *   block_table       device int32 [batch, max_blocks_per_seq]: position t of
+ *                     sequence b lives in page block_table[b][t / page_size],
+ *                     row t % page_size
+ *   kv_lens           device int32 [batch]; 0 is allowed and yields zeros
+ *   q, out            [batch, num_heads, head_dim]
+ *   page_size         a multiple of 16 rows
+ *   max_kv_len        host upper bound of kv_lens, <= max_blocks_per_seq * page_size
+ * Only the first ceil(kv_lens[b] / page_size) entries of a row are read; page
+ * ids outside [0, num_pages) read as zero rows, and rows of the last page
+ * past kv_lens[b] are never used, whatever they hold.  No reference
+ * counterpart: the reference keeps one contiguous cache per layer
+ * (runtime/kv_cache.cpp:14-37) and lists paging as future work (README.md:31). */
+FR_API int fr_decode_attn_paged(const void* q, const void* k_pages, const void* v_pages,
+                                const int* block_table, const int* kv_lens, void* out,
+                                int batch, int num_heads, int num_kv_heads, int head_dim,
+                                int page_size, int num_pages, int max_blocks_per_seq,
+                                int max_kv_len, void* stream);
+
 /* Partial attention over positions [0, kv_len) of the given cache view:
  * writes one log-sum-exp state per query head instead of an output, for
  * KV ranges that are split across GPUs.  No reference counterpart.

@@ -144,6 +144,23 @@ def batched_f64(q: np.ndarray, ks: list, vs: list, lens) -> np.ndarray:
     return np.stack([decode_f64(q[b], ks[b], vs[b], int(lens[b])) for b in range(q.shape[0])])
 
 
+def paged_f64(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarray, block_table: np.ndarray,
+              lens, page_size: int) -> np.ndarray:
+    """Paged cache [num_pages, page_size, Hkv, D]: sequence b's position t is
+    row t % page_size of page block_table[b, t // page_size].  The rows are
+    gathered back into one contiguous cache per sequence (the reference's
+    layer-view layout, runtime/kv_cache.cpp:29-37) and decoded with
+    batched_f64."""
+    ks, vs = [], []
+    for b, n in enumerate(lens):
+        n = int(n)
+        t = np.arange(n)
+        pages = block_table[b, t // page_size]
+        ks.append(k_pages[pages, t % page_size])
+        vs.append(v_pages[pages, t % page_size])
+    return batched_f64(q, ks, vs, lens)
+
+
 def partial_f64(q: np.ndarray, k: np.ndarray, v: np.ndarray, begin: int, end: int):
     """(m, l, acc) over positions [begin, end), base 2: m = max_t s_t log2(e)/sqrt(D)."""
     H, D = q.shape

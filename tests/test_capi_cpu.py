@@ -72,6 +72,17 @@ def test_validation_before_any_cuda_call(lib):
                                       None) == _lib.FR_ERR_INVALID_ARG
     assert lib.fr_decode_attn_batched(fake, fake + 8, fake, fake, fake, fake, 2, 8, 2, 64, 100, 16,
                                       None) == _lib.FR_ERR_MISALIGNED
+    # paged: page_size a multiple of 16, the table must cover max_kv_len, pool < 2^31 rows
+    paged = lambda *a: lib.fr_decode_attn_paged(fake, fake, fake, fake, fake, fake, *a, None)  # noqa: E731
+    assert paged(2, 8, 2, 64, 8, 10, 4, 32) == _lib.FR_ERR_INVALID_ARG
+    assert paged(2, 8, 2, 64, 24, 10, 4, 64) == _lib.FR_ERR_INVALID_ARG
+    assert paged(2, 8, 2, 64, 16, 10, 4, 65) == _lib.FR_ERR_INVALID_ARG
+    assert paged(2, 8, 2, 64, 16, 0, 4, 64) == _lib.FR_ERR_INVALID_ARG
+    assert paged(0, 8, 2, 64, 16, 10, 4, 64) == _lib.FR_ERR_INVALID_ARG
+    assert paged(2, 8, 2, 64, 1 << 16, 1 << 15, 4, 64) == _lib.FR_ERR_INVALID_ARG
+    assert paged(2, 8, 2, 96, 16, 10, 4, 64) == _lib.FR_ERR_UNSUPPORTED
+    assert lib.fr_decode_attn_paged(fake, fake + 8, fake, fake, fake, fake, 2, 8, 2, 64, 16, 10,
+                                    4, 64, None) == _lib.FR_ERR_MISALIGNED
     assert lib.fr_decode_attn_partial(fake, fake, fake, -1, fake, fake, 8, 2, 64, None) == \
         _lib.FR_ERR_INVALID_ARG
     assert lib.fr_lse_merge(fake, fake, 0, fake, 8, 64, None) == _lib.FR_ERR_INVALID_ARG

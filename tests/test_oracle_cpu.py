@@ -154,3 +154,22 @@ def test_half_conversion_bit_exact():
             want = np.array([x], np.float64).astype(np.float16).view(np.uint16)[0]
             assert got == want, (x, hex(got), hex(want))
             assert lib.oracle_half_to_float(int(want)) == np.float32(np.float16(x))
+
+
+def test_paged_layout_round_trip():
+    """paginate() + paged_f64 (gather by block table) reproduce the contiguous
+    per-sequence caches exactly, whatever order the pages were handed out in."""
+    rng = np.random.default_rng(21)
+    lens = np.array([1, 15, 16, 17, 100, 0, 64], np.int32)
+    ks = [W.normal_fp16(rng, (int(n), 2, 64)) for n in lens]
+    vs = [W.normal_fp16(rng, (int(n), 2, 64)) for n in lens]
+    q = W.normal_fp16(rng, (len(lens), 8, 64))
+    for page in (16, 48):
+        kp, vp, table = W.paginate(ks, vs, page, seed=page, spare_pages=3)
+        assert np.isnan(kp.astype(np.float32)).any()          # unowned rows are NaN
+        for b, n in enumerate(lens):
+            t = np.arange(int(n))
+            assert np.array_equal(kp[table[b, t // page], t % page], ks[b])
+            assert (table[b, -(-int(n) // page):] == -1).all()
+        assert np.array_equal(O.paged_f64(q, kp, vp, table, lens, page),
+                              O.batched_f64(q, ks, vs, lens))
