@@ -60,9 +60,8 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", choices=["ours", "reference", "refgpu"], default="ours",
-                    help="reference = the reference's CPU implementation; refgpu = the "
-                         "reference's own v4 GPU kernel built for sm_100a (oracle/_ref)")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours",
+                    help="reference = the reference's CPU implementation")
     ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg3p", "cfg4"], default="cfg2")
     ap.add_argument("--page-size", type=int, default=16, help="cfg3p page rows (multiple of 16)")
     ap.add_argument("--page-order", choices=["shuffled", "sequential"], default="shuffled",
@@ -742,60 +741,6 @@ def run_reference(args, rank, world):
     })
 
 
-def run_refgpu(args, rank, world):
-    """The reference's decode_attn_v4_flash (kernels/attention_decode.cu:418-556),
-    compiled for sm_100a from its sources into oracle/_ref, timed on the cfg2
-    workload exactly like our arm (eager launches, L2 flushed per group)."""
-    if rank != 0:
-        return
-    import torch
-    from oracle import oracle as O
-    ref = O.load_ref()
-    if ref is None:
-        emit({"impl": "refgpu", "unavailable": "oracle/_ref not built"})
-        return
-    device = torch.device("cuda", 0)
-    wl = Cfg2(torch, 0, device)
-    stream = torch.cuda.Stream(device)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
-    sp = stream.cuda_stream
-
-    def group(kv):
-        for l in range(wl.L):
-            ref.ref_decode_attn_v4_flash(wl.q[l].data_ptr(), wl.cache[l, 0].data_ptr(),
-                                         wl.cache[l, 1].data_ptr(), wl.out[l].data_ptr(),
-                                         wl.H, wl.HKV, wl.D, kv, sp)
-
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            for kv in wl.groups:
-                group(kv)
-    torch.cuda.synchronize()
-    K = args.steps
-    ms = {kv: 0.0 for kv in wl.groups}
-    with torch.cuda.stream(stream):
-        for _ in range(K):
-            for i, kv in enumerate(wl.groups):
-                flush.fill_(i & 0xFF)
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                group(kv)
-                e1.record(stream)
-                e1.synchronize()
-                ms[kv] += e0.elapsed_time(e1)
-    total = sum(ms.values())
-    sweep = {str(kv): {"us_per_call": round(ms[kv] * 1e3 / (K * wl.L), 3),
-                       "gbs": round(wl.call_bytes(kv) * K * wl.L / (ms[kv] * 1e-3) / 1e9, 1)}
-             for kv in wl.groups}
-    emit({"metric": METRIC, "impl": "refgpu", "value": round(wl.bytes_per_step() * K / (total * 1e-3) / 1e9, 2),
-          "unit": UNIT, "n_gpus": 1, "steps": K, "warmup": args.warmup,
-          "ms_per_step": round(total / K, 4), "higher_is_better": True,
-          "config": {"workload": wl.config()["workload"], "sweep": sweep,
-                     "kernel": "reference decode_attn_v4_flash, sm_100a build of its own sources "
-                               "(-O3 --use_fast_math), eager launches"}})
-
-
 def main():
     args = parse_args()
     rank, local_rank, world = dist_env()
@@ -803,9 +748,6 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     if args.impl == "reference":
         run_reference(args, rank, world)
-        return
-    if args.impl == "refgpu":
-        run_refgpu(args, rank, world)
         return
     import torch
     import torch.distributed as dist

@@ -37,6 +37,8 @@ SIGNATURES = {
                                   ctypes.c_longlong, _vp]),
     "fr_rope_tables": (_i, [_vp, _vp, _i, _i, ctypes.c_float, ctypes.c_float]),
     "fr_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
+    "fr_qkv_bias_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i,
+                                     _i, _i, _i, _vp]),
     "fr_prefill_attn": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "fr_reserve_workspace": (_i, [ctypes.c_size_t]),
     "fr_decode_workspace_size": (ctypes.c_size_t, [_i, _i, _i, _i, _i]),

@@ -144,6 +144,18 @@ def rope_append(q, k, v, k_cache, v_cache, cos_tab, sin_tab, seq_len: int, num_h
         seq_len, num_heads, num_kv_heads, head_dim, pos_offset, _stream(stream)))
 
 
+def qkv_bias_rope_append(q, k, v, q_bias, k_bias, v_bias, k_cache, v_cache, cos_tab, sin_tab,
+                         seq_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                         pos_offset: int, stream=None) -> None:
+    """q/k/v += bias (None = no bias), RoPE on q/k, KV append: one launch in
+    place of runtime/executor.cpp:135-152's six."""
+    lib = load()
+    check("fr_qkv_bias_rope_append", lib.fr_qkv_bias_rope_append(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(q_bias), _ptr(k_bias), _ptr(v_bias), _ptr(k_cache),
+        _ptr(v_cache), _ptr(cos_tab), _ptr(sin_tab), seq_len, num_heads, num_kv_heads, head_dim,
+        pos_offset, _stream(stream)))
+
+
 def reserve_workspace(nbytes: int) -> None:
     lib = load()
     check("fr_reserve_workspace", lib.fr_reserve_workspace(nbytes))

@@ -591,25 +591,41 @@ int fr_rope_tables(float* cos_tab, float* sin_tab, int max_seq_len, int head_dim
     return FR_OK;
 }
 
-int fr_rope_append(void* q, void* k, const void* v, void* k_cache, void* v_cache,
-                   const float* cos_tab, const float* sin_tab, int seq_len, int num_heads,
-                   int num_kv_heads, int head_dim, int pos_offset, void* stream) {
+int fr_qkv_bias_rope_append(void* q, void* k, void* v, const void* q_bias, const void* k_bias,
+                            const void* v_bias, void* k_cache, void* v_cache,
+                            const float* cos_tab, const float* sin_tab, int seq_len,
+                            int num_heads, int num_kv_heads, int head_dim, int pos_offset,
+                            void* stream) {
     if (!q || !k || !v || !k_cache || !v_cache || !cos_tab || !sin_tab || seq_len <= 0 ||
         pos_offset < 0)
         return FR_ERR_INVALID_ARG;
     int rc = check_heads(num_heads, num_kv_heads, head_dim);
     if (rc != FR_OK) return rc;
     if (!aligned(v, 16) || !aligned(v_cache, 16) || !aligned(q, 2) || !aligned(k, 2) ||
-        !aligned(k_cache, 2))
+        !aligned(k_cache, 2) || !aligned(v_bias, 16) || !aligned(q_bias, 2) ||
+        !aligned(k_bias, 2))
         return FR_ERR_MISALIGNED;
-    fr::rope_append_kernel<<<seq_len, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<__half*>(q), static_cast<__half*>(k), static_cast<const __half*>(v),
-        static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), cos_tab, sin_tab,
-        num_heads, num_kv_heads, head_dim, pos_offset);
+    const dim3 grid(seq_len, (fr::rope_items(num_heads, num_kv_heads, head_dim) +
+                              fr::kRopeThreads - 1) / fr::kRopeThreads);
+    fr::rope_append_kernel<<<grid, fr::kRopeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<__half*>(q), static_cast<__half*>(k), static_cast<__half*>(v),
+        static_cast<const __half*>(q_bias), static_cast<const __half*>(k_bias),
+        static_cast<const __half*>(v_bias), static_cast<__half*>(k_cache),
+        static_cast<__half*>(v_cache), cos_tab, sin_tab, num_heads, num_kv_heads, head_dim,
+        pos_offset);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return FR_OK;
+}
+
+// Without biases v is only read (the kernel writes v back only when biasing it).
+int fr_rope_append(void* q, void* k, const void* v, void* k_cache, void* v_cache,
+                   const float* cos_tab, const float* sin_tab, int seq_len, int num_heads,
+                   int num_kv_heads, int head_dim, int pos_offset, void* stream) {
+    return fr_qkv_bias_rope_append(q, k, const_cast<void*>(v), nullptr, nullptr, nullptr,
+                                   k_cache, v_cache, cos_tab, sin_tab, seq_len, num_heads,
+                                   num_kv_heads, head_dim, pos_offset, stream);
 }
 
 int fr_prefill_attn(const void* q, const void* k, const void* v, void* out, int seq_len,

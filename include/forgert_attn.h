@@ -165,6 +165,20 @@ FR_API int fr_rope_append(void* q, void* k, const void* v, void* k_cache, void* 
                    const float* cos_tab, const float* sin_tab, int seq_len, int num_heads,
                    int num_kv_heads, int head_dim, int pos_offset, void* stream);
 
+/* The same prologue with the projection biases folded in: q += q_bias,
+ * k += k_bias, v += v_bias (one fp16 round-to-nearest addition per element,
+ * as bias_add_broadcast, kernels/elementwise.cu:81-98), then RoPE on q and k
+ * and the KV append, in one launch.  Replaces the six launches of
+ * runtime/executor.cpp:135-152 (three bias adds, rope_v2_fused, two copies).
+ * Any bias may be NULL (no add); q_bias [num_heads*head_dim], k_bias and
+ * v_bias [num_kv_heads*head_dim] fp16, v_bias 16-byte aligned.  q and k are
+ * left rotated and v biased in place, as the reference sequence leaves them. */
+FR_API int fr_qkv_bias_rope_append(void* q, void* k, void* v, const void* q_bias,
+                                   const void* k_bias, const void* v_bias, void* k_cache,
+                                   void* v_cache, const float* cos_tab, const float* sin_tab,
+                                   int seq_len, int num_heads, int num_kv_heads, int head_dim,
+                                   int pos_offset, void* stream);
+
 /* Causal prefill attention: query position s attends to positions 0..s.
  * Replaces prefill_attn_causal (kernels/attention.cuh:76-82; definition
  * kernels/attention_decode.cu:563-619).

@@ -29,6 +29,10 @@
  *                            theta = pos / (base^(2f/D) * scale), in fp64.
  *   oracle_rope_append       rope_kernel_v2_fused, kernels/rope.cu:162-191, plus
  *                            the KV append of runtime/executor.cpp:145-152.
+ *   oracle_qkv_bias_rope_append
+ *                            the same preceded by the q/k/v bias adds of
+ *                            runtime/executor.cpp:135-137 (bias_broadcast_kernel,
+ *                            kernels/elementwise.cu:81-91).
  *
  * fp16 data is passed as raw binary16 bit patterns (uint16_t).
  */
@@ -275,6 +279,37 @@ static void rope_inplace(uint16_t* x, const float* cos_tab, const float* sin_tab
                 row[f + half_d] = oracle_double_to_half((double)r1);
             }
         }
+}
+
+/* x[t, :] += bias[:] in fp16: the exact sum rounded once to nearest-even,
+ * which is what __hadd computes (bias_broadcast_kernel,
+ * kernels/elementwise.cu:81-91).  A NULL bias leaves x unchanged. */
+static void bias_add_f16(uint16_t* x, const uint16_t* bias, int rows, int width) {
+    if (!bias) return;
+    for (int t = 0; t < rows; t++)
+        for (int d = 0; d < width; d++) {
+            uint16_t* e = x + (size_t)t * width + d;
+            *e = oracle_double_to_half((double)h2f(*e) + (double)h2f(bias[d]));
+        }
+}
+
+/* The reference's decode prologue with projection biases
+ * (runtime/executor.cpp:135-152): q/k/v += bias, RoPE on q and k, then the
+ * k/v rows appended to the cache at pos_offset + t.  q, k, v are updated in
+ * place like the reference's activation buffers. */
+void oracle_qkv_bias_rope_append(uint16_t* q, uint16_t* k, uint16_t* v, const uint16_t* q_bias,
+                                 const uint16_t* k_bias, const uint16_t* v_bias,
+                                 uint16_t* k_cache, uint16_t* v_cache, const float* cos_tab,
+                                 const float* sin_tab, int seq_len, int num_heads,
+                                 int num_kv_heads, int head_dim, int pos_offset) {
+    bias_add_f16(q, q_bias, seq_len, num_heads * head_dim);
+    bias_add_f16(k, k_bias, seq_len, num_kv_heads * head_dim);
+    bias_add_f16(v, v_bias, seq_len, num_kv_heads * head_dim);
+    rope_inplace(q, cos_tab, sin_tab, seq_len, num_heads, head_dim, pos_offset);
+    rope_inplace(k, cos_tab, sin_tab, seq_len, num_kv_heads, head_dim, pos_offset);
+    const size_t row = (size_t)num_kv_heads * head_dim;
+    memcpy(k_cache + (size_t)pos_offset * row, k, sizeof(uint16_t) * row * seq_len);
+    memcpy(v_cache + (size_t)pos_offset * row, v, sizeof(uint16_t) * row * seq_len);
 }
 
 /* RoPE on q and k in place, then k/v rows appended to the cache at

@@ -64,6 +64,8 @@ def load_oracle() -> ctypes.CDLL:
                                                ctypes.c_double, ctypes.c_double]
         lib.oracle_rope_append.argtypes = [_u16p, _u16p, _u16p, _u16p, _u16p, _f32p, _f32p] + \
             [ctypes.c_int] * 5
+        lib.oracle_qkv_bias_rope_append.argtypes = [_u16p] * 8 + [_f32p, _f32p] + \
+            [ctypes.c_int] * 5
         lib.oracle_half_to_float.argtypes = [ctypes.c_uint16]
         lib.oracle_half_to_float.restype = ctypes.c_float
         lib.oracle_double_to_half.argtypes = [ctypes.c_double]
@@ -85,6 +87,7 @@ def load_ref() -> ctypes.CDLL | None:
         lib.ref_decode_attn_v4_flash.argtypes = [vp, vp, vp, vp] + [ctypes.c_int] * 4 + [vp]
         lib.ref_prefill_attn_causal.argtypes = [vp, vp, vp, vp] + [ctypes.c_int] * 4 + [vp]
         lib.ref_rope_v2_fused.argtypes = [vp, vp, vp, vp] + [ctypes.c_int] * 5 + [vp]
+        lib.ref_bias_add_broadcast.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int, vp]
         lib.ref_run_kernel_tests.restype = ctypes.c_int
         _ref_lib = lib
     return _ref_lib
@@ -318,6 +321,27 @@ def c_rope_append(q, k, v, k_cache, v_cache, cos_t, sin_t, pos_offset: int):
                            _ptr(vc, _u16p), _ptr(ct, _f32p), _ptr(st, _f32p), T, H, Hkv, D,
                            pos_offset)
     return (qh.view(np.float16), kh.view(np.float16), kc.view(np.float16), vc.view(np.float16))
+
+
+def c_qkv_bias_rope_append(q, k, v, q_bias, k_bias, v_bias, k_cache, v_cache, cos_t, sin_t,
+                           pos_offset: int):
+    """Biased + rotated (q, k), biased v and updated (k_cache, v_cache) copies
+    (fp16); a None bias is skipped."""
+    lib = load_oracle()
+    T, H, D = q.shape
+    Hkv = k.shape[1]
+    bufs = [np.ascontiguousarray(a, np.float16).copy().view(np.uint16)
+            for a in (q, k, v, k_cache, v_cache)]
+    qh, kh, vh, kc, vc = bufs
+    bias = [None if b is None else np.ascontiguousarray(b, np.float16).view(np.uint16)
+            for b in (q_bias, k_bias, v_bias)]
+    bp = [None if b is None else _ptr(b, _u16p) for b in bias]
+    ct = np.ascontiguousarray(cos_t, np.float32)
+    st = np.ascontiguousarray(sin_t, np.float32)
+    lib.oracle_qkv_bias_rope_append(_ptr(qh, _u16p), _ptr(kh, _u16p), _ptr(vh, _u16p), bp[0],
+                                    bp[1], bp[2], _ptr(kc, _u16p), _ptr(vc, _u16p),
+                                    _ptr(ct, _f32p), _ptr(st, _f32p), T, H, Hkv, D, pos_offset)
+    return tuple(b.view(np.float16) for b in (qh, kh, vh, kc, vc))
 
 
 def ref_cpu_decode_attn(q: np.ndarray, k: np.ndarray, v: np.ndarray) -> np.ndarray:

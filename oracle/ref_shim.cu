@@ -71,6 +71,11 @@ void ref_rope_v2_fused(void* q, void* k, const float* cos_tab, const float* sin_
                   num_q_heads, num_kv_heads, head_dim, pos_offset, static_cast<cudaStream_t>(stream));
 }
 
+void ref_bias_add_broadcast(void* out, const void* bias, int seq_len, int hidden, void* stream) {
+    bias_add_broadcast(static_cast<__half*>(out), static_cast<const __half*>(bias), seq_len,
+                       hidden, static_cast<cudaStream_t>(stream));
+}
+
 // The reference's own kernel test program (14 checks); returns its exit code.
 int ref_run_kernel_tests(void) { return forgert_reference_test_main(); }
 

@@ -235,6 +235,37 @@ def test_rope_append_matches_oracle():
     assert np.array_equal(vcd.cpu().numpy(), vco)
 
 
+@pytest.mark.parametrize("T,H,Hkv,D,which", [(1, 14, 2, 64, "qkv"), (5, 12, 2, 128, "qkv"),
+                                             (1, 28, 4, 128, "q"), (3, 8, 8, 64, "kv")])
+def test_qkv_bias_rope_append_matches_oracle(T, H, Hkv, D, which):
+    rng = np.random.default_rng(9 + T + D)
+    S, pos = 300, 200
+    q = W.normal_fp16(rng, (T, H, D))
+    k = W.normal_fp16(rng, (T, Hkv, D))
+    v = W.normal_fp16(rng, (T, Hkv, D))
+    biases = [W.normal_fp16(rng, (n * D,)) if c in which else None
+              for n, c in ((H, "q"), (Hkv, "k"), (Hkv, "v"))]
+    kc = W.normal_fp16(rng, (S, Hkv, D))
+    vc = W.normal_fp16(rng, (S, Hkv, D))
+    cos_d, sin_d = A.rope_precompute_tables(S, D, W.ROPE_THETA)
+    ct, st = O.c_rope_tables(S, D, W.ROPE_THETA)
+    qd, kd, vd, kcd, vcd = dev(q), dev(k), dev(v), dev(kc), dev(vc)
+    bd = [None if b is None else dev(b) for b in biases]
+    A.qkv_bias_rope_append(qd, kd, vd, bd[0], bd[1], bd[2], kcd, vcd, cos_d, sin_d, T, H, Hkv, D,
+                           pos)
+    torch.cuda.synchronize()
+    assert A.device_error() == 0
+    qo, ko, vo, kco, vco = O.c_qkv_bias_rope_append(q, k, v, *biases, kc, vc, ct, st, pos)
+    # one fp16 ulp where the rotation is involved (FMA contraction of a*c - b*s)
+    for got, want, what in [(qd, qo, "q"), (kd, ko, "k"), (kcd, kco, "k_cache")]:
+        g = got.cpu().numpy().astype(np.float64)
+        w = want.astype(np.float64)
+        assert np.all(np.abs(g - w) <= np.abs(w) * 2 ** -10 + 1e-7), what
+    # the bias add alone is exact
+    assert np.array_equal(vd.cpu().numpy().view(np.uint16), vo.view(np.uint16))
+    assert np.array_equal(vcd.cpu().numpy().view(np.uint16), vco.view(np.uint16))
+
+
 def test_against_reference_gpu_kernel():
     ref = O.load_ref()
     if ref is None:

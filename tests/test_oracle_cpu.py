@@ -173,3 +173,32 @@ def test_paged_layout_round_trip():
             assert (table[b, -(-int(n) // page):] == -1).all()
         assert np.array_equal(O.paged_f64(q, kp, vp, table, lens, page),
                               O.batched_f64(q, ks, vs, lens))
+
+
+def test_bias_prologue_oracle():
+    """q/k/v bias add is one fp16 RN addition (numpy's float16 add rounds the
+    exact sum once, as __hadd does); with no biases the prologue is exactly
+    the RoPE + append oracle."""
+    rng = np.random.default_rng(31)
+    T, H, Hkv, D, S, pos = 3, 14, 2, 64, 40, 30
+    q = W.normal_fp16(rng, (T, H, D))
+    k = W.normal_fp16(rng, (T, Hkv, D))
+    v = W.normal_fp16(rng, (T, Hkv, D))
+    bq = W.normal_fp16(rng, (H * D,))
+    bk = W.normal_fp16(rng, (Hkv * D,))
+    bv = W.normal_fp16(rng, (Hkv * D,))
+    kc = W.normal_fp16(rng, (S, Hkv, D))
+    vc = W.normal_fp16(rng, (S, Hkv, D))
+    ct, st = O.c_rope_tables(S, D, W.ROPE_THETA)
+    got = O.c_qkv_bias_rope_append(q, k, v, bq, bk, bv, kc, vc, ct, st, pos)
+    qb = (q + bq.reshape(H, D)).astype(np.float16)
+    kb = (k + bk.reshape(Hkv, D)).astype(np.float16)
+    vb = (v + bv.reshape(Hkv, D)).astype(np.float16)
+    want = O.c_rope_append(qb, kb, vb, kc, vc, ct, st, pos)
+    for g, w in zip((got[0], got[1], got[3], got[4]), want):
+        assert np.array_equal(g.view(np.uint16), w.view(np.uint16))
+    assert np.array_equal(got[2].view(np.uint16), vb.view(np.uint16))
+    plain = O.c_qkv_bias_rope_append(q, k, v, None, None, None, kc, vc, ct, st, pos)
+    ref = O.c_rope_append(q, k, v, kc, vc, ct, st, pos)
+    for g, w in zip((plain[0], plain[1], plain[3], plain[4]), ref):
+        assert np.array_equal(g.view(np.uint16), w.view(np.uint16))
