@@ -66,6 +66,8 @@ def parse_args():
     ap.add_argument("--page-size", type=int, default=16, help="cfg3p page rows (multiple of 16)")
     ap.add_argument("--page-order", choices=["shuffled", "sequential"], default="shuffled",
                     help="cfg3p: pages handed out in a seeded random order, or in order")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="cfg4 at N > 1: in-kernel peer exchange or NCCL all-gather")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of graphs")
     ap.add_argument("--no-overlap", action="store_true",
                     help="disable launch overlap (pre-wait K/V prefetch under PDL)")
@@ -394,13 +396,16 @@ class Cfg3Paged(Cfg3):
 class Cfg4:
     """Qwen2-7B long context: one sequence, kv_len 131072, H28 Hkv4 D128.
     One GPU: a plain fr_decode_attn call.  N GPUs: each rank holds a
-    contiguous KV range, computes its (m, l, acc) states, one NCCL all-gather
-    exchanges them and every rank merges.  Total work is fixed ("strong")."""
+    contiguous KV range.  exchange "peer" (default): one
+    fr_decode_attn_exchange kernel per rank computes its states, stores them
+    into every rank's exchange buffer over NVLink and merges what arrives;
+    exchange "nccl": partial kernel, NCCL all-gather of the states, merge
+    kernel.  Total work is fixed ("strong")."""
 
     H, HKV, D, T = 28, 4, 128, 131072
     scaling = "strong"
 
-    def __init__(self, torch, rank: int, world: int, device):
+    def __init__(self, torch, rank: int, world: int, device, exchange: str = "peer"):
         from forgert_b200 import sharding as SH
         self.torch = torch
         self.world = world
@@ -415,10 +420,16 @@ class Cfg4:
         self.q.normal_(generator=torch.Generator(device=device).manual_seed(33))
         self.out = torch.empty_like(self.q)
         self.groups = ["step"]
-        self.dec = SH.LongContextDecoder(self.H, self.HKV, self.D, device) if world > 1 else None
-        # N > 1: the NCCL all-gather is captured in the same CUDA graph as the
-        # partial and merge kernels (graphs are released before the process
-        # group is destroyed).
+        self.exchange = exchange if world > 1 else "none"
+        if world == 1:
+            self.dec = None
+        elif exchange == "peer":
+            self.dec = SH.PeerExchangeDecoder(self.H, self.HKV, self.D, device)
+        else:
+            # the NCCL all-gather is captured in the same CUDA graph as the
+            # partial and merge kernels (graphs are released before the
+            # process group is destroyed)
+            self.dec = SH.LongContextDecoder(self.H, self.HKV, self.D, device)
         self.graphable = True
         self.my_bytes = W.decode_bytes([self.n], self.H, self.HKV, self.D)
         self.q_host = self.q.cpu().pin_memory()
@@ -461,8 +472,11 @@ class Cfg4:
     def config(self):
         return {
             "workload": "cfg4: Qwen2-7B-shape long-context decode attention, 1 sequence, "
-                        "kv_len 131072, KV range split across GPUs + NCCL all-gather of "
-                        "(m, l, acc) + LSE merge",
+                        "kv_len 131072, KV range split across GPUs, (m, l, acc) states "
+                        "exchanged and merged",
+            "exchange": {"none": "single GPU", "peer": "in-kernel peer stores over NVLink + "
+                         "merge (fr_decode_attn_exchange)", "nccl": "NCCL all-gather + merge "
+                         "kernel"}[self.exchange],
             "model": "Qwen2-7B attention shape (random data)",
             "global_batch": 1, "num_heads": self.H, "num_kv_heads": self.HKV,
             "head_dim": self.D, "kv_len": self.T, "kv_rows_this_rank": self.n,
@@ -484,7 +498,7 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     elif args.workload == "cfg3p":
         wl = Cfg3Paged(torch, rank, world, device, args.page_size, args.page_order)
     else:
-        wl = Cfg4(torch, rank, world, device)
+        wl = Cfg4(torch, rank, world, device, args.exchange)
     stream = torch.cuda.Stream(device)
     # Decode-step launch overlap: the attention kernel may stream K/V rows
     # older than the newest one while the preceding kernel finishes.
@@ -597,6 +611,9 @@ def run_ours(args, torch, dist, rank, local_rank, world):
                "how": "per call: H2D q from pinned host, fr_decode_attn, D2H out to pinned host; "
                       "eager launches, CUDA events, L2 flushed per kv_len group"}
 
+    close = getattr(getattr(wl, "dec", None), "close", None)
+    if close is not None:
+        close()                          # collective: every rank frees its exchange buffer
     if rank != 0:
         return
     peak, peak_kind = peaks()
@@ -620,7 +637,7 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     par = {"cfg2": f"dp{world} (one sequence per GPU)",
            "cfg3": f"{world} GPUs, (sequence, kv head) units by LPT, no collective",
            "cfg3p": f"{world} GPUs, sequences by LPT, no collective",
-           "cfg4": f"{world} GPUs, KV range split, all-gather of states"}[args.workload]
+           "cfg4": f"{world} GPUs, KV range split, states exchanged ({args.exchange})"}[args.workload]
     cfg.update({"parallelism": par, "graph": use_graph,
                 "launch_overlap": not args.no_overlap, "sweep": sweep})
     line = {

@@ -41,6 +41,14 @@ SIGNATURES = {
                                      _i, _i, _i, _vp]),
     "fr_prefill_attn": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "fr_reserve_workspace": (_i, [ctypes.c_size_t]),
+    "fr_exchange_bytes": (ctypes.c_size_t, [_i, _i, _i]),
+    "fr_exchange_alloc": (_i, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _vp]),
+    "fr_exchange_open": (_i, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "fr_exchange_close": (_i, [_vp]),
+    "fr_exchange_free": (_i, [_vp]),
+    "fr_exchange_reset": (_i, [_vp, ctypes.c_size_t, _vp]),
+    "fr_decode_attn_exchange": (_i, [_vp, _vp, _vp, _i, _vp, _i, _i, _i,
+                                     ctypes.POINTER(ctypes.c_void_p), _i, _i, _vp]),
     "fr_decode_workspace_size": (ctypes.c_size_t, [_i, _i, _i, _i, _i]),
     "fr_get_device_error": (_i, [_i, ctypes.POINTER(_i)]),
     "fr_last_cuda_error": (_i, []),

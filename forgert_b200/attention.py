@@ -156,6 +156,35 @@ def qkv_bias_rope_append(q, k, v, q_bias, k_bias, v_bias, k_cache, v_cache, cos_
         pos_offset, _stream(stream)))
 
 
+EXCHANGE_HEADER_BYTES = 256          # u32 epoch, u32 done
+
+
+def exchange_layout(num_heads: int, head_dim: int, world: int) -> dict:
+    """Byte offsets inside one rank's exchange buffer (fr_exchange_bytes):
+    header, then ml [2][world][H][2] and acc [2][world][H][D] 8-byte words
+    indexed [call parity][source rank]; a word is (call epoch << 32) | fp32
+    bits."""
+    ml = EXCHANGE_HEADER_BYTES
+    acc = ml + 2 * world * num_heads * 2 * 8
+    return {"header": 0, "ml": ml, "acc": acc,
+            "bytes": acc + 2 * world * num_heads * head_dim * 8}
+
+
+def decode_attn_exchange(q, k_local, v_local, local_kv_len: int, out, num_heads: int,
+                         num_kv_heads: int, head_dim: int, bufs, rank: int, world: int,
+                         stream=None) -> None:
+    """This GPU's KV range + the in-kernel exchange of states with the other
+    ranks (bufs: every rank's exchange buffer as seen from here)."""
+    import ctypes
+
+    lib = load()
+    arr = (ctypes.c_void_p * world)(*[_ptr(b) for b in bufs])
+    check("fr_decode_attn_exchange", lib.fr_decode_attn_exchange(
+        _ptr(q), _ptr(k_local) if local_kv_len else None, _ptr(v_local) if local_kv_len else None,
+        local_kv_len, _ptr(out), num_heads, num_kv_heads, head_dim, arr, rank, world,
+        _stream(stream)))
+
+
 def reserve_workspace(nbytes: int) -> None:
     lib = load()
     check("fr_reserve_workspace", lib.fr_reserve_workspace(nbytes))

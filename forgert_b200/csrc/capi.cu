@@ -15,6 +15,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -353,6 +354,40 @@ int plan_for(DeviceState* st, int head_dim, int batch, int num_kv_heads, int gro
     return FR_OK;
 }
 
+// Clusters of `cl` CTAs (or CTAs, cl == 1) of the split kernel that can be
+// resident on the device at once.
+int resident_clusters(int D, int nt, int cl, DeviceState* st) {
+    const int slot = (D == 64 ? 0 : 2) + (nt - 1);
+    if (cl == 1) return st->sm_count * std::max(1, st->occupancy[slot]);
+    const void* fn = nullptr;
+    size_t smem = 0;
+    auto pick = [&](auto kfn, size_t bytes) { fn = reinterpret_cast<const void*>(kfn); smem = bytes; };
+    if (D == 64) {
+        if (nt == 1) pick(cl == 8 ? kernel_ptr<64, 1, 8>() : cl == 4 ? kernel_ptr<64, 1, 4>() : kernel_ptr<64, 1, 2>(), SmemOf<64, 1>::kBytes);
+        else pick(cl == 8 ? kernel_ptr<64, 2, 8>() : cl == 4 ? kernel_ptr<64, 2, 4>() : kernel_ptr<64, 2, 2>(), SmemOf<64, 2>::kBytes);
+    } else {
+        if (nt == 1) pick(cl == 8 ? kernel_ptr<128, 1, 8>() : cl == 4 ? kernel_ptr<128, 1, 4>() : kernel_ptr<128, 1, 2>(), SmemOf<128, 1>::kBytes);
+        else pick(cl == 8 ? kernel_ptr<128, 2, 8>() : cl == 4 ? kernel_ptr<128, 2, 4>() : kernel_ptr<128, 2, 2>(), SmemOf<128, 2>::kBytes);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, cl, 1);
+    cfg.blockDim = dim3(32 * (kConsumerWarps + 1), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = cl;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
 // Shared driver of the decode-family entry points.  `p` carries the tensor
 // maps and the sequence geometry.
 //   final_out != nullptr : write fp16 output
@@ -391,6 +426,21 @@ int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* 
         pl.num_splits = (tiles + tps - 1) / tps;
     }
     const bool fused = units * cl <= kMaxUnits;      // one counter per (unit, cluster rank)
+    if (p.xworld > 0) {
+        // The exchange waits inside the kernel for the other GPUs, which wait
+        // for this one: every cluster of the grid must be resident at once.
+        if (!fused) return FR_ERR_UNSUPPORTED;
+        const int resident = resident_clusters(D, pl.nt, cl, st);
+        const long long max_splits_res = (long long)(resident / std::max<long long>(1, units)) * cl;
+        if (max_splits_res < cl) return FR_ERR_UNSUPPORTED;
+        if (pl.num_splits > max_splits_res) {
+            const int kTile = tile_rows();
+            const int tiles = std::max(1, (max_kv_len + kTile - 1) / kTile);
+            const int tps = (int)((tiles + max_splits_res - 1) / max_splits_res);
+            pl.split_len = tps * kTile;
+            pl.num_splits = (tiles + tps - 1) / tps;
+        }
+    }
     const int splits = (pl.num_splits + cl - 1) / cl * cl;     // pads at most one cluster
     p.G = group;
     p.split_len = pl.split_len;
@@ -402,7 +452,7 @@ int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* 
     p.evict_normal = evict_normal;
     const bool pdl = s != nullptr;
     const long long rows = (long long)batch * p.H;
-    if (final_out && splits == 1) {
+    if (final_out && splits == 1 && p.xworld == 0) {
         p.write_final = 1;
         p.out = final_out;
     } else {
@@ -420,6 +470,11 @@ int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* 
         }
     }
     dim3 grid(p.Hkv * pl.head_groups, splits, batch);
+    static const int trace_plan = env_int("FORGERT_TRACE_PLAN", 0);
+    if (trace_plan)
+        std::fprintf(stderr, "[forgert] plan D=%d batch=%d units=%lld splits=%d split_len=%d "
+                     "cluster=%d fused=%d xworld=%d grid=(%u,%u,%u)\n", D, batch, units, splits,
+                     pl.split_len, cl, (int)fused, p.xworld, grid.x, grid.y, grid.z);
     rc = D == 64 ? launch_split_any<64>(p, pl.nt, cl, grid, s, pdl)
                  : launch_split_any<128>(p, pl.nt, cl, grid, s, pdl);
     if (rc != FR_OK || p.write_final || p.counters) return rc;
@@ -567,6 +622,92 @@ int fr_lse_merge_strided(const float* states_ml, const float* states_acc, int nu
                                   nullptr, 0, s)
                : launch_merge<128>(states_ml, states_acc, num_states, ms, num_heads, o, nullptr,
                                    nullptr, 0, s);
+}
+
+size_t fr_exchange_bytes(int num_heads, int head_dim, int world) {
+    if (num_heads <= 0 || (head_dim != 64 && head_dim != 128) || world <= 0 ||
+        world > fr::kMaxRanks)
+        return 0;
+    return fr::XLayout::bytes(world, num_heads, head_dim);
+}
+
+int fr_exchange_alloc(size_t bytes, void** buf, void* ipc_handle) {
+    if (!buf || !ipc_handle || bytes < fr::XLayout::kHeader) return FR_ERR_INVALID_ARG;
+    *buf = nullptr;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_fail(e);
+    e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e);
+    }
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    *buf = p;
+    return FR_OK;
+}
+
+int fr_exchange_open(const void* ipc_handle, void** peer_buf) {
+    if (!ipc_handle || !peer_buf) return FR_ERR_INVALID_ARG;
+    *peer_buf = nullptr;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof(h));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e);
+    *peer_buf = p;
+    return FR_OK;
+}
+
+int fr_exchange_close(void* peer_buf) {
+    if (!peer_buf) return FR_ERR_INVALID_ARG;
+    cudaError_t e = cudaIpcCloseMemHandle(peer_buf);
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
+
+int fr_exchange_free(void* buf) {
+    if (!buf) return FR_ERR_INVALID_ARG;
+    cudaError_t e = cudaFree(buf);
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
+
+// Zeroes the whole buffer: the epoch restarts at 0, so words tagged by the
+// calls before the reset must not survive it.
+int fr_exchange_reset(void* buf, size_t bytes, void* stream) {
+    if (!buf || bytes < fr::XLayout::kHeader) return FR_ERR_INVALID_ARG;
+    cudaError_t e = cudaMemsetAsync(buf, 0, bytes, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
+
+int fr_decode_attn_exchange(const void* q, const void* k_local, const void* v_local,
+                            int local_kv_len, void* out, int num_heads, int num_kv_heads,
+                            int head_dim, void* const* bufs, int rank, int world, void* stream) {
+    if (!q || !out || !bufs || local_kv_len < 0 || world <= 0 || world > fr::kMaxRanks ||
+        rank < 0 || rank >= world)
+        return FR_ERR_INVALID_ARG;
+    if (local_kv_len > 0 && (!k_local || !v_local)) return FR_ERR_INVALID_ARG;
+    for (int j = 0; j < world; ++j)
+        if (!bufs[j]) return FR_ERR_INVALID_ARG;
+    int rc = check_heads(num_heads, num_kv_heads, head_dim);
+    if (rc != FR_OK) return rc;
+    if ((local_kv_len > 0 && (!aligned(k_local, 16) || !aligned(v_local, 16))) ||
+        !aligned(q, 4) || !aligned(out, 4))
+        return FR_ERR_MISALIGNED;
+    for (int j = 0; j < world; ++j)
+        if (!aligned(bufs[j], 256)) return FR_ERR_MISALIGNED;
+    DecodeParams p = base_params(q, num_heads, num_kv_heads);
+    rc = encode_pair(&p, k_local, v_local, head_dim, num_kv_heads, local_kv_len);
+    if (rc != FR_OK) return rc;
+    p.kv_len = local_kv_len;
+    for (int j = 0; j < world; ++j) p.xbuf[j] = bufs[j];
+    p.xrank = rank;
+    p.xworld = world;
+    p.xrows = num_heads;
+    return run_decode(p, head_dim, 1, std::max(1, local_kv_len), static_cast<__half*>(out),
+                      nullptr, nullptr, 1, static_cast<cudaStream_t>(stream));
 }
 
 int fr_rope_tables(float* cos_tab, float* sin_tab, int max_seq_len, int head_dim, float base,

@@ -45,6 +45,8 @@
 
 namespace fr {
 
+constexpr int kMaxRanks = 8;        // GPUs of one cross-GPU exchange
+
 struct DecodeParams {
     CUtensorMap kmap;            // K view [rows][Hkv][D/64][64] (see file header)
     CUtensorMap vmap;            // V view, same geometry
@@ -83,7 +85,60 @@ struct DecodeParams {
     int page_size;               // rows per page, multiple of 16
     int page_box;                // rows per TMA box: gcd(page_size, TILE)
     int num_pages;               // pool size; other ids read as zeros
+    // Cross-GPU exchange (xworld > 0, fused path only): the final (m, l, acc)
+    // state slices go to every rank's exchange buffer (XLayout) and each rank
+    // merges the xworld states of every head row into `out`.
+    void* xbuf[kMaxRanks];       // exchange buffer of each rank ([xrank] = this GPU's)
+    int xrank, xworld;
+    int xrows;                   // head rows per state (B * H)
 };
+
+// Layout of one rank's exchange buffer (bytes from its base):
+//   [0, 256)   header: u32 epoch (calls completed), u32 done (CTAs of the
+//              current call that finished)
+//   then ml  [2 parities][world][rows][2] u64 words
+//   then acc [2 parities][world][rows][D] u64 words
+// Every word is (epoch of the call that wrote it) << 32 | fp32 bits, stored
+// by the source rank in one 8-byte access; the reader waits until a word's
+// tag equals its own epoch.  Call e uses parity e & 1; a rank can start call
+// e + 2 only after every rank finished call e + 1, so a parity is never
+// overwritten while it is read.  All zero (tag 0) is "nothing written".
+struct XLayout {
+    static constexpr size_t kHeader = 256;
+    __host__ __device__ static size_t bytes(int world, int rows, int D) {
+        return kHeader + size_t(2) * world * rows * (2 + D) * sizeof(uint64_t);
+    }
+    __host__ __device__ static uint32_t* header(void* base) {
+        return reinterpret_cast<uint32_t*>(base);
+    }
+    __host__ __device__ static uint64_t* ml(void* base, int par, int src, int world, int rows) {
+        uint64_t* m0 = reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(base) + kHeader);
+        return m0 + (size_t)(par * world + src) * rows * 2;
+    }
+    __host__ __device__ static uint64_t* acc(void* base, int par, int src, int world, int rows,
+                                             int D) {
+        uint64_t* a0 = ml(base, 0, 0, world, rows) + size_t(2) * world * rows * 2;
+        return a0 + (size_t)(par * world + src) * rows * D;
+    }
+};
+
+// Waits (bounded) until the word at `addr` carries tag `epoch`; returns its
+// value.  `ok` is cleared on timeout, after which no further waits are made.
+__device__ __forceinline__ float x_wait_word(const uint64_t* addr, uint64_t w, uint32_t epoch,
+                                             bool& ok) {
+    if (uint32_t(w >> 32) != epoch && ok) {
+        const unsigned long long t0 = globaltimer_ns();
+        do {
+            w = ld_relaxed_sys_u64(addr);
+            if (uint32_t(w >> 32) == epoch) break;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                ok = false;
+                break;
+            }
+        } while (true);
+    }
+    return __uint_as_float(uint32_t(w));
+}
 
 __device__ __forceinline__ void record_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
@@ -603,6 +658,26 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     const int e_begin = crank * per;
     const int e_end = min(nel, e_begin + per);
     const bool state_out = p.out_ml != nullptr;
+    // Cross-GPU exchange: this call's epoch (the header advances only after
+    // every CTA of the grid has finished) selects the buffer parity.
+    const bool xmode = p.xworld > 0;
+    const uint32_t xepoch = xmode ? __ldcg(XLayout::header(p.xbuf[p.xrank])) + 1u : 0u;
+    const int xpar = int(xepoch & 1u);
+    // Stores one element of a final state into every rank's exchange buffer
+    // (tagged words, see XLayout).
+    auto x_push = [&](size_t hrow, int d, float m, float l, float a) {
+        const uint64_t tag = uint64_t(xepoch) << 32;
+        for (int j = 0; j < p.xworld; ++j) {
+            void* base = p.xbuf[j];
+            st_relaxed_sys_u64(XLayout::acc(base, xpar, p.xrank, p.xworld, p.xrows, D) + hrow * D + d,
+                               tag | __float_as_uint(a));
+            if (d == 0) {
+                uint64_t* mlp = XLayout::ml(base, xpar, p.xrank, p.xworld, p.xrows) + 2 * hrow;
+                st_relaxed_sys_u64(mlp, tag | __float_as_uint(m));
+                st_relaxed_sys_u64(mlp + 1, tag | __float_as_uint(l));
+            }
+        }
+    };
 
     if constexpr (CL > 1) cluster_sync_all();       // every CTA's state is in its smem
     {
@@ -636,7 +711,9 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
             }
             const size_t hrow = head_base + hj;
             if (ncl == 1) {
-                if (state_out) {
+                if (xmode) {
+                    x_push(hrow, d, mstar, l, a);
+                } else if (state_out) {
                     p.out_acc[hrow * D + d] = a;
                     if (d == 0) { p.out_ml[2 * hrow] = mstar; p.out_ml[2 * hrow + 1] = l; }
                 } else {
@@ -696,7 +773,9 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                     }
                     m = cm;
                 }
-                if (state_out) {
+                if (xmode) {
+                    x_push(hrow, d, m, l, a);
+                } else if (state_out) {
                     p.out_acc[hrow * D + d] = a;
                     if (d == 0) { p.out_ml[2 * hrow] = m; p.out_ml[2 * hrow + 1] = l; }
                 } else {
@@ -706,7 +785,69 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
             if (threadIdx.x == 0) p.counters[unit * CL + crank] = 0;   // ready for the next call
         }
     }
+
+    // ------------------------------------------------ cross-GPU exchange
+    // The CTAs that pushed a final slice wait until every rank's words for
+    // their slice carry this call's tag in the local buffer (all loads of an
+    // element issued first, then only late words are polled), and merge the
+    // slice over the ranks.
+    if (xmode && (ncl == 1 || st_flag[0])) {
+        void* xb = p.xbuf[p.xrank];
+        bool ok = true;
+        for (int e = e_begin + threadIdx.x; e < e_end; e += blockDim.x) {
+            const int hj = e / D;
+            const int d = e - hj * D;
+            const size_t hrow = head_base + hj;
+            uint64_t wm[kMaxRanks], wl[kMaxRanks], wa[kMaxRanks];
+#pragma unroll
+            for (int j = 0; j < kMaxRanks; ++j) {
+                if (j < p.xworld) {
+                    const uint64_t* mlp = XLayout::ml(xb, xpar, j, p.xworld, p.xrows) + 2 * hrow;
+                    wm[j] = ld_relaxed_sys_u64(mlp);
+                    wl[j] = ld_relaxed_sys_u64(mlp + 1);
+                    wa[j] = ld_relaxed_sys_u64(XLayout::acc(xb, xpar, j, p.xworld, p.xrows, D) +
+                                               hrow * D + d);
+                }
+            }
+            float m = -INFINITY, l = 0.f, a = 0.f;
+#pragma unroll
+            for (int j = 0; j < kMaxRanks; ++j) {
+                if (j < p.xworld) {
+                    const uint64_t* mlp = XLayout::ml(xb, xpar, j, p.xworld, p.xrows) + 2 * hrow;
+                    const float mj = x_wait_word(mlp, wm[j], xepoch, ok);
+                    const float lj = x_wait_word(mlp + 1, wl[j], xepoch, ok);
+                    const float aj = x_wait_word(
+                        XLayout::acc(xb, xpar, j, p.xworld, p.xrows, D) + hrow * D + d, wa[j],
+                        xepoch, ok);
+                    const float mn = fmaxf(m, mj);
+                    const float mu = (mn == -INFINITY) ? 0.f : mn;
+                    const float c_old = fast_exp2(m - mu), c_new = fast_exp2(mj - mu);
+                    a = fmaf(a, c_old, aj * c_new);
+                    l = fmaf(l, c_old, lj * c_new);
+                    m = mn;
+                }
+            }
+            p.out[hrow * D + d] = __float2half_rn(l > 0.f ? a / l : 0.f);
+        }
+        if (!ok) record_error(p.err, kDevTimeoutPeer);
+    }
     if constexpr (CL > 1) cluster_wait_acquire();   // peers done reading this CTA's smem
+    if (xmode) {
+        // The last CTA of the grid to get here advances the epoch; every CTA
+        // read it above (ordered before its count by the barrier and fence).
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            uint32_t* hdr = XLayout::header(p.xbuf[p.xrank]);
+            const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
+            if (atomicAdd(&hdr[1], 1u) == total - 1) {
+                __threadfence();
+                hdr[1] = 0u;
+                hdr[0] = xepoch;
+                __threadfence();
+            }
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------

@@ -20,6 +20,7 @@ enum DeviceError : int {
     kDevOk = 0,
     kDevTimeoutFull = 1,   // consumer gave up waiting for a stage to land
     kDevTimeoutEmpty = 2,  // producer gave up waiting for a stage to drain
+    kDevTimeoutPeer = 3,   // cross-GPU exchange: the other ranks' states never all arrived
 };
 
 // Wall-clock budget of one bounded wait (ns).  Real waits last microseconds;
@@ -190,6 +191,20 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
     asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;"
                  : "=r"(old) : "l"(addr), "r"(v) : "memory");
     return old;
+}
+
+// 8-byte system-scope relaxed store / load.  An aligned 8-byte access is
+// single-copy atomic, so a 4-byte value stored together with a 4-byte tag is
+// seen by another GPU either whole or not at all: the tag tells the reader
+// that the value has arrived (no fence or separate flag needed).
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* addr, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(addr), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* addr) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+    return v;
 }
 
 // Programmatic dependent launch: wait until the grids this one depends on

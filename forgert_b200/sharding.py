@@ -147,3 +147,82 @@ class LongContextDecoder:
             self.partial_fn(q, k_local, v_local, local_len, ml, acc, stream)
             self.exchange()
             self.merge_fn(self.gathered, self.world, out, stream)
+
+
+class PeerExchangeDecoder:
+    """KV-range-sharded decode of one sequence with the exchange inside the
+    kernel (fr_decode_attn_exchange): each rank's split kernel stores its
+    (m, l, acc) states into every rank's exchange buffer over NVLink and
+    merges the states it receives - no collective call on the data path.
+
+    Set-up (collective, once): each rank allocates its buffer, the 64-byte
+    CUDA IPC handles are all-gathered through `group` (any backend), and each
+    rank opens the others'.  close() is collective too: it waits at a barrier
+    so that no rank frees a buffer another may still write.
+    """
+
+    def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int, device, group=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from ._lib import check, load
+
+        self.lib = load()
+        self.dist, self.group = dist, group
+        self.H, self.Hkv, self.D = num_heads, num_kv_heads, head_dim
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.nbytes = self.lib.fr_exchange_bytes(num_heads, head_dim, self.world)
+        if not self.nbytes:
+            raise ValueError("unsupported exchange shape")
+        with torch.cuda.device(device):
+            buf = ctypes.c_void_p()
+            handle = (ctypes.c_char * 64)()
+            check("fr_exchange_alloc", self.lib.fr_exchange_alloc(self.nbytes, ctypes.byref(buf),
+                                                                  handle))
+            self.local = buf.value
+            handles = [None] * self.world
+            if self.world > 1:
+                dist.all_gather_object(handles, bytes(handle), group=group)
+            ptrs, self.opened = [], []
+            for j in range(self.world):
+                if j == self.rank:
+                    ptrs.append(self.local)
+                    continue
+                peer = ctypes.c_void_p()
+                h = (ctypes.c_char * 64).from_buffer_copy(handles[j])
+                check("fr_exchange_open", self.lib.fr_exchange_open(h, ctypes.byref(peer)))
+                ptrs.append(peer.value)
+                self.opened.append(peer.value)
+        self.bufs = (ctypes.c_void_p * self.world)(*ptrs)
+        self.closed = False
+
+    def __call__(self, q, k_local, v_local, local_len: int, out, stream=None) -> None:
+        from ._lib import check
+        from .attention import _ptr, _stream
+        check("fr_decode_attn_exchange", self.lib.fr_decode_attn_exchange(
+            _ptr(q), _ptr(k_local) if local_len else None, _ptr(v_local) if local_len else None,
+            local_len, _ptr(out), self.H, self.Hkv, self.D, self.bufs, self.rank, self.world,
+            _stream(stream)))
+
+    def reset(self, stream=None) -> None:
+        """After a timed-out exchange: zero this rank's counters and epoch
+        (every rank must do it before the next call)."""
+        from ._lib import check
+        from .attention import _stream
+        check("fr_exchange_reset", self.lib.fr_exchange_reset(self.local, self.nbytes,
+                                                              _stream(stream)))
+
+    def close(self) -> None:
+        if self.closed:
+            return
+        import torch
+        torch.cuda.synchronize()
+        if self.world > 1:
+            self.dist.barrier(group=self.group)
+        for p in self.opened:
+            self.lib.fr_exchange_close(p)
+        self.lib.fr_exchange_free(self.local)
+        self.closed = True

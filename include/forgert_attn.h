@@ -147,6 +147,42 @@ FR_API int fr_lse_merge_strided(const float* states_ml, const float* states_acc,
                                 long long ml_state_stride, long long acc_state_stride,
                                 void* stream);
 
+/* ---- Cross-GPU long-context decode (KV range split across GPUs) ----------
+ * One sequence's cache rows are split in contiguous ranges, one per GPU (one
+ * process per GPU).  fr_decode_attn_exchange computes this GPU's split-KV
+ * state and, in the same kernel, stores its (m, l, acc) slices into every
+ * GPU's exchange buffer over NVLink/NVSwitch (plain peer stores), waits
+ * (bounded) until all GPUs' states of a head group have arrived in its own
+ * buffer and merges them into out: the all-gather + log-sum-exp merge of a
+ * KV-range split, without a collective library call.  Every GPU gets the
+ * full result.  No reference counterpart (the reference runs on one GPU).
+ *
+ * Set-up, once per process group: every rank calls fr_exchange_alloc (one
+ * buffer of fr_exchange_bytes bytes, zeroed, on the current device) and
+ * sends its 64-byte IPC handle to the others (e.g. an all-gather of bytes),
+ * then opens each peer's handle with fr_exchange_open.  bufs[j] is rank j's
+ * buffer as seen from this process (bufs[rank] = the local one).
+ * All ranks must make the same sequence of calls with the same num_heads,
+ * num_kv_heads and head_dim (local_kv_len may differ); a call returns once
+ * launched.  Each state word is stored with the call's sequence number in
+ * one 8-byte access, so a receiver needs no fence or flag: it waits until the
+ * words it reads carry its own call number.  If a peer does not take part,
+ * the wait ends after about a second with FR_ERR_TIMEOUT from
+ * fr_get_device_error; the exchange state is then inconsistent and every rank
+ * must fr_exchange_reset its buffer (stream ordered) before the next call.
+ *   q, out     [num_heads, head_dim] fp16 (the same q on every rank)
+ *   k_local, v_local  this GPU's rows [local_kv_len, num_kv_heads, head_dim] */
+FR_API size_t fr_exchange_bytes(int num_heads, int head_dim, int world);
+FR_API int fr_exchange_alloc(size_t bytes, void** buf, void* ipc_handle /* 64 bytes out */);
+FR_API int fr_exchange_open(const void* ipc_handle, void** peer_buf);
+FR_API int fr_exchange_close(void* peer_buf);
+FR_API int fr_exchange_free(void* buf);
+FR_API int fr_exchange_reset(void* buf, size_t bytes, void* stream);
+FR_API int fr_decode_attn_exchange(const void* q, const void* k_local, const void* v_local,
+                                   int local_kv_len, void* out, int num_heads, int num_kv_heads,
+                                   int head_dim, void* const* bufs, int rank, int world,
+                                   void* stream);
+
 /* RoPE cos/sin tables [max_seq_len, head_dim/2] fp32 into caller-allocated
  * device buffers: theta(pos, f) = pos / (base^(2f/head_dim) * scale), evaluated
  * in fp64 on the host and rounded once.  Synchronous, like the reference.

@@ -4,6 +4,9 @@
   rank computes its (m, l, acc) states with fr_decode_attn_partial, one NCCL
   all-gather exchanges them, fr_lse_merge_strided merges.  Every rank's
   output must match the CPU oracle over the whole range.
+* Long context, exchange in the kernel: fr_decode_attn_exchange stores each
+  rank's states into every rank's buffer (CUDA IPC mappings, plain peer
+  stores) and merges what arrives; eager and CUDA-graph replays.
 * Batched: (sequence, kv head) units are sharded by LPT; each rank decodes its
   own units from its own KV pool with no collective.  The outputs are
   gathered afterwards (verification only) and compared with the oracle.
@@ -65,7 +68,30 @@ def _rank_main(rank, world, port, result_q):
             for _ in range(2):                       # twice: counters/workspace reused
                 dec(qd, kd, vd, e - b, out, s)
         torch.cuda.synchronize()
-        errs["long"] = O.max_errors(out.cpu().numpy(), O.decode_f64(q, k, v), EPS)
+        exact = O.decode_f64(q, k, v)
+        errs["long"] = O.max_errors(out.cpu().numpy(), exact, EPS)
+
+        # ---- long context, exchange inside the kernel (peer stores over NVLink)
+        px = SH.PeerExchangeDecoder(H, Hkv, D, dev)
+        outp = torch.full((H, D), float("nan"), dtype=torch.float16, device=dev)
+        with torch.cuda.stream(s):
+            for _ in range(3):                       # epochs 1..3: both buffer parities
+                px(qd, kd, vd, e - b, outp, s)
+        torch.cuda.synchronize()
+        assert A.device_error() == 0
+        errs["long_peer"] = O.max_errors(outp.cpu().numpy(), exact, EPS)
+        # and as a CUDA graph, replayed
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            px(qd, kd, vd, e - b, outp, s)
+        for _ in range(3):
+            outp.fill_(float("nan"))
+            g.replay()
+        torch.cuda.synchronize()
+        assert A.device_error() == 0
+        errs["long_peer_graph"] = O.max_errors(outp.cpu().numpy(), exact, EPS)
+        del g
+        px.close()
 
         # ---- batched: units by LPT, own pool per rank, no collective
         rng = np.random.default_rng(42)
