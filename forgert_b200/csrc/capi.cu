@@ -52,6 +52,8 @@ struct DeviceState {
     size_t ws_bytes = 0;
     uint32_t attr_done = 0;      // bit per kernel instantiation: smem attribute set
     int occupancy[8] = {0};      // CTAs/SM per instantiation (0 = not queried)
+    int resident[4][5] = {{-1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1},
+                          {-1, -1, -1, -1, -1}};   // co-resident clusters per (slot, log2 size)
 };
 
 std::mutex g_mu;
@@ -173,6 +175,8 @@ int set_smem_attr() {
     for (auto fn : {kernel_ptr<D, NT, CL, false>(), kernel_ptr<D, NT, CL, true>()}) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(SmemOf<D, NT>::kBytes));
+        if (e == cudaSuccess && CL > 8)        // 16-CTA clusters are a non-portable size
+            e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return cuda_fail(e);
     }
     return FR_OK;
@@ -186,6 +190,7 @@ int prepare_kernel(DeviceState* st) {
         if (rc == FR_OK) rc = set_smem_attr<D, NT, 2>();
         if (rc == FR_OK) rc = set_smem_attr<D, NT, 4>();
         if (rc == FR_OK) rc = set_smem_attr<D, NT, 8>();
+        if (rc == FR_OK) rc = set_smem_attr<D, NT, 16>();
         if (rc != FR_OK) return rc;
         int n = 0;
         cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
@@ -230,6 +235,7 @@ int launch_split(const DecodeParams& p, dim3 grid, cudaStream_t s, bool pdl) {
 template <int D, int NT, bool PAGED>
 int launch_split_nt(const DecodeParams& p, int cl, dim3 grid, cudaStream_t s, bool pdl) {
     switch (cl) {
+        case 16: return launch_split<D, NT, 16, PAGED>(p, grid, s, pdl);
         case 8: return launch_split<D, NT, 8, PAGED>(p, grid, s, pdl);
         case 4: return launch_split<D, NT, 4, PAGED>(p, grid, s, pdl);
         case 2: return launch_split<D, NT, 2, PAGED>(p, grid, s, pdl);
@@ -328,6 +334,19 @@ int max_splits() {
     return v;
 }
 
+// FORGERT_ONE_CLUSTER_TILES: the most tiles per CTA for which a unit is
+// covered by one 16-CTA cluster (default 4; 0 = never).
+// FORGERT_MAX_CLUSTER: largest cluster of the multi-cluster plans (8 or 16).
+int max_cluster() {
+    static const int v = env_int("FORGERT_MAX_CLUSTER", 8);
+    return v;
+}
+
+int one_cluster_tiles() {
+    static const int v = env_int("FORGERT_ONE_CLUSTER_TILES", 4);
+    return v;
+}
+
 int cluster_min_splits() {
     static const int v = env_int("FORGERT_CLUSTER_MIN_SPLITS", kClusterCtas);
     return v;
@@ -356,18 +375,31 @@ int plan_for(DeviceState* st, int head_dim, int batch, int num_kv_heads, int gro
 
 // Clusters of `cl` CTAs (or CTAs, cl == 1) of the split kernel that can be
 // resident on the device at once.
+int query_resident_clusters(int D, int nt, int cl, DeviceState* st);
+
 int resident_clusters(int D, int nt, int cl, DeviceState* st) {
+    const int slot = (D == 64 ? 0 : 2) + (nt - 1);
+    const int li = cl >= 16 ? 4 : cl >= 8 ? 3 : cl >= 4 ? 2 : cl >= 2 ? 1 : 0;
+    int& cached = st->resident[slot][li];
+    if (cached < 0) cached = query_resident_clusters(D, nt, cl, st);
+    return cached;
+}
+
+int query_resident_clusters(int D, int nt, int cl, DeviceState* st) {
     const int slot = (D == 64 ? 0 : 2) + (nt - 1);
     if (cl == 1) return st->sm_count * std::max(1, st->occupancy[slot]);
     const void* fn = nullptr;
     size_t smem = 0;
     auto pick = [&](auto kfn, size_t bytes) { fn = reinterpret_cast<const void*>(kfn); smem = bytes; };
+    auto choose = [&](auto k16, auto k8, auto k4, auto k2, size_t bytes) {
+        pick(cl == 16 ? k16 : cl == 8 ? k8 : cl == 4 ? k4 : k2, bytes);
+    };
     if (D == 64) {
-        if (nt == 1) pick(cl == 8 ? kernel_ptr<64, 1, 8>() : cl == 4 ? kernel_ptr<64, 1, 4>() : kernel_ptr<64, 1, 2>(), SmemOf<64, 1>::kBytes);
-        else pick(cl == 8 ? kernel_ptr<64, 2, 8>() : cl == 4 ? kernel_ptr<64, 2, 4>() : kernel_ptr<64, 2, 2>(), SmemOf<64, 2>::kBytes);
+        if (nt == 1) choose(kernel_ptr<64, 1, 16>(), kernel_ptr<64, 1, 8>(), kernel_ptr<64, 1, 4>(), kernel_ptr<64, 1, 2>(), SmemOf<64, 1>::kBytes);
+        else choose(kernel_ptr<64, 2, 16>(), kernel_ptr<64, 2, 8>(), kernel_ptr<64, 2, 4>(), kernel_ptr<64, 2, 2>(), SmemOf<64, 2>::kBytes);
     } else {
-        if (nt == 1) pick(cl == 8 ? kernel_ptr<128, 1, 8>() : cl == 4 ? kernel_ptr<128, 1, 4>() : kernel_ptr<128, 1, 2>(), SmemOf<128, 1>::kBytes);
-        else pick(cl == 8 ? kernel_ptr<128, 2, 8>() : cl == 4 ? kernel_ptr<128, 2, 4>() : kernel_ptr<128, 2, 2>(), SmemOf<128, 2>::kBytes);
+        if (nt == 1) choose(kernel_ptr<128, 1, 16>(), kernel_ptr<128, 1, 8>(), kernel_ptr<128, 1, 4>(), kernel_ptr<128, 1, 2>(), SmemOf<128, 1>::kBytes);
+        else choose(kernel_ptr<128, 2, 16>(), kernel_ptr<128, 2, 8>(), kernel_ptr<128, 2, 4>(), kernel_ptr<128, 2, 2>(), SmemOf<128, 2>::kBytes);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1, cl, 1);
@@ -413,11 +445,25 @@ int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* 
     // clusters (batched calls hide that merge behind other units).
     const int cmin = cluster_min_splits();
     int cl = 1;
-    if (cmin > 0 && pl.num_splits >= cmin) {
+    // Short ranges of a few units: one cluster of 16 per unit with at most
+    // one_cluster_tiles() tiles per CTA needs no merge across clusters, which
+    // costs more than the extra tiles (single-sequence calls only).
+    const int kTileRows = tile_rows();
+    const int tiles_u = std::max(1, (max_kv_len + kTileRows - 1) / kTileRows);
+    const int oct = one_cluster_tiles();
+    const bool one_cluster16 = waves == 1 && oct > 0 && tiles_u > 8 && tiles_u <= 16 * oct &&
+                               units * 16 <= st->sm_count &&
+                               resident_clusters(D, pl.nt, 16, st) >= units;
+    if (one_cluster16) {
+        cl = 16;
+        const int tps = (tiles_u + 15) / 16;
+        pl.split_len = tps * kTileRows;
+        pl.num_splits = (tiles_u + tps - 1) / tps;
+    } else if (cmin > 0 && pl.num_splits >= cmin) {
         const int want = pl.num_splits;
-        cl = 8;
-        for (int c : {4, 2})
-            if ((want / c) * c * 20 >= (want / cl) * cl * 21) cl = c;   // > 5% more splits
+        cl = (max_cluster() >= 16 && want >= 16 && resident_clusters(D, pl.nt, 16, st) > 0) ? 16 : 8;
+        for (int c : {8, 4, 2})
+            if (c < cl && (want / c) * c * 20 >= (want / cl) * cl * 21) cl = c;   // > 5% more splits
         const int kTile = tile_rows();
         const int tiles = std::max(1, (max_kv_len + kTile - 1) / kTile);
         const int nsp = std::max(cl, want / cl * cl);
