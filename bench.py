@@ -717,7 +717,7 @@ def cpu_baseline_cfg2(budget_s: float):
         runner.run()
         reps += 1
         el = time.perf_counter() - t0
-        if el >= budget_s or reps >= 50:
+        if el >= budget_s or reps >= 2000:
             break
     return {"value": round(runner.bytes() * reps / el / 1e9, 4), "unit": UNIT,
             "cores": runner.threads, "kind": runner.kind,
