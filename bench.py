@@ -68,6 +68,8 @@ def parse_args():
                     help="cfg3p: pages handed out in a seeded random order, or in order")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="cfg4 at N > 1: in-kernel peer exchange or NCCL all-gather")
+    ap.add_argument("--layers", type=int, default=1,
+                    help="cfg4: layer caches decoded back to back per step (default 1 call)")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of graphs")
     ap.add_argument("--no-overlap", action="store_true",
                     help="disable launch overlap (pre-wait K/V prefetch under PDL)")
@@ -400,27 +402,32 @@ class Cfg4:
     fr_decode_attn_exchange kernel per rank computes its states, stores them
     into every rank's exchange buffer over NVLink and merges what arrives;
     exchange "nccl": partial kernel, NCCL all-gather of the states, merge
-    kernel.  Total work is fixed ("strong")."""
+    kernel.  `layers` > 1 runs that many layer caches back to back in one
+    CUDA graph (a decode step's attention calls) instead of a single call.
+    Total work is fixed ("strong")."""
 
     H, HKV, D, T = 28, 4, 128, 131072
     scaling = "strong"
 
-    def __init__(self, torch, rank: int, world: int, device, exchange: str = "peer"):
+    def __init__(self, torch, rank: int, world: int, device, exchange: str = "peer",
+                 layers: int = 1):
         from forgert_b200 import sharding as SH
         self.torch = torch
         self.world = world
+        self.L = max(1, layers)
         b, e = SH.kv_ranges(self.T, world)[rank]
         self.n = e - b
         g = torch.Generator(device=device)
         g.manual_seed(3 + 1000 * rank)
-        self.k = torch.empty((max(self.n, 1), self.HKV, self.D), dtype=torch.float16,
+        self.k = torch.empty((self.L, max(self.n, 1), self.HKV, self.D), dtype=torch.float16,
                              device=device).normal_(generator=g)
         self.v = torch.empty_like(self.k).normal_(generator=g)
-        self.q = torch.empty((self.H, self.D), dtype=torch.float16, device=device)
+        self.q = torch.empty((self.L, self.H, self.D), dtype=torch.float16, device=device)
         self.q.normal_(generator=torch.Generator(device=device).manual_seed(33))
         self.out = torch.empty_like(self.q)
         self.groups = ["step"]
         self.exchange = exchange if world > 1 else "none"
+        self.align_ranks = world > 1
         if world == 1:
             self.dec = None
         elif exchange == "peer":
@@ -436,29 +443,30 @@ class Cfg4:
         self.out_host = torch.empty_like(self.q_host).pin_memory()
 
     def bytes_per_group(self, key) -> int:
-        return self.my_bytes
+        return self.my_bytes * self.L
 
     def bytes_per_step(self) -> int:
-        return self.my_bytes
+        return self.my_bytes * self.L
 
     def job_bytes(self) -> int:
-        return W.decode_bytes([self.T], self.H, self.HKV, self.D)
+        return W.decode_bytes([self.T], self.H, self.HKV, self.D) * self.L
 
     def call_bytes(self, key) -> int:
         return self.my_bytes
 
     def calls_per_group(self) -> int:
-        return 1
+        return self.L
 
     def workspace_bytes(self, A) -> int:
         return A.decode_workspace_size(1, self.H, self.HKV, self.D, max(self.n, 1))
 
     def run_group(self, A, key, stream) -> None:
-        if self.dec is None:
-            A.decode_attn_v4_flash(self.q, self.k, self.v, self.out, self.H, self.HKV, self.D,
-                                   self.n, stream)
-        else:
-            self.dec(self.q, self.k, self.v, self.n, self.out, stream)
+        for l in range(self.L):
+            if self.dec is None:
+                A.decode_attn_v4_flash(self.q[l], self.k[l], self.v[l], self.out[l], self.H,
+                                       self.HKV, self.D, self.n, stream)
+            else:
+                self.dec(self.q[l], self.k[l], self.v[l], self.n, self.out[l], stream)
 
     def run_group_e2e(self, A, key, stream) -> None:
         self.q.copy_(self.q_host, non_blocking=True)
@@ -466,7 +474,7 @@ class Cfg4:
         self.out_host.copy_(self.out, non_blocking=True)
 
     def e2e_bytes(self):
-        n = self.H * self.D * 2
+        n = self.L * self.H * self.D * 2
         return n, n
 
     def config(self):
@@ -480,7 +488,10 @@ class Cfg4:
             "model": "Qwen2-7B attention shape (random data)",
             "global_batch": 1, "num_heads": self.H, "num_kv_heads": self.HKV,
             "head_dim": self.D, "kv_len": self.T, "kv_rows_this_rank": self.n,
+            "layers": self.L,
             "l2": "flushed (256 MiB write) before each step; events exclude the flush",
+            "rank_alignment": "N > 1: one-element NCCL all-reduce after the flush, before "
+                              "the events (ranks start each call together)",
         }
 
 
@@ -498,7 +509,7 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     elif args.workload == "cfg3p":
         wl = Cfg3Paged(torch, rank, world, device, args.page_size, args.page_order)
     else:
-        wl = Cfg4(torch, rank, world, device, args.exchange)
+        wl = Cfg4(torch, rank, world, device, args.exchange, args.layers)
     stream = torch.cuda.Stream(device)
     # Decode-step launch overlap: the attention kernel may stream K/V rows
     # older than the newest one while the preceding kernel finishes.
@@ -532,9 +543,18 @@ def run_ours(args, torch, dist, rank, local_rank, world):
         torch.cuda.synchronize()
         launches_per_step = lib.fr_launch_count() - c0
 
+    # Workloads whose ranks exchange data inside the timed call (cfg4 at N > 1)
+    # start each call together: a one-element all-reduce after the flush,
+    # outside the events, so the per-rank flush and launch skew is not timed
+    # as waiting for the slowest rank.
+    align = torch.zeros(1, dtype=torch.float32, device=device) \
+        if world > 1 and getattr(wl, "align_ranks", False) else None
+
     def step(events):
         for i, kv in enumerate(wl.groups):
             flush.fill_(i & 0xFF)
+            if align is not None:
+                dist.all_reduce(align)
             if events is not None:
                 events[i][0].record(stream)
             if use_graph:
@@ -595,6 +615,8 @@ def run_ours(args, torch, dist, rank, local_rank, world):
             for k in range(Ke):
                 for i, kv in enumerate(wl.groups):
                     flush.fill_(i & 0xFF)
+                    if align is not None:
+                        dist.all_reduce(align)
                     ev2[k][i][0].record(stream)
                     wl.run_group_e2e(A, kv, stream)
                     ev2[k][i][1].record(stream)

@@ -235,6 +235,45 @@ def test_rope_append_matches_oracle():
     assert np.array_equal(vcd.cpu().numpy(), vco)
 
 
+@pytest.mark.parametrize("H,Hkv,D,T", [(28, 4, 128, 50000), (12, 2, 128, 77777),
+                                       (14, 2, 64, 200003), (28, 4, 128, 131072)])
+def test_long_single_sequence_repeated_and_replayed(H, Hkv, D, T):
+    """Long single sequences (many tiles per CTA, several clusters per kv
+    head): eager calls in a row, then CUDA-graph replays of three calls with
+    launch overlap on; the merge counters must be back at zero after every
+    call."""
+    q, k, v = W.decode_inputs(200 + T % 97, H, Hkv, D, T)
+    exact = O.decode_f64(q, k, v)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    lib = A.load()
+    s = torch.cuda.Stream()
+    out = nan_like(qd)
+    for _ in range(3):
+        out.fill_(float("nan"))
+        with torch.cuda.stream(s):
+            A.decode_attn_v4_flash(qd, kd, vd, out, H, Hkv, D, T, s)
+        torch.cuda.synchronize()
+        assert A.device_error() == 0
+        assert_close(out.cpu().numpy(), exact, what=f"long eager T={T}")
+    outs = [nan_like(qd) for _ in range(3)]
+    lib.fr_set_launch_overlap(1)
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for o in outs:
+                A.decode_attn_v4_flash(qd, kd, vd, o, H, Hkv, D, T, s)
+        for _ in range(3):
+            for o in outs:
+                o.fill_(float("nan"))
+            g.replay()
+            torch.cuda.synchronize()
+            assert A.device_error() == 0
+            for o in outs:
+                assert_close(o.cpu().numpy(), exact, what=f"long graph T={T}")
+    finally:
+        lib.fr_set_launch_overlap(0)
+
+
 @pytest.mark.parametrize("T,H,Hkv,D,which", [(1, 14, 2, 64, "qkv"), (5, 12, 2, 128, "qkv"),
                                              (1, 28, 4, 128, "q"), (3, 8, 8, 64, "kv")])
 def test_qkv_bias_rope_append_matches_oracle(T, H, Hkv, D, which):
