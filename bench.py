@@ -220,13 +220,6 @@ class Cfg2:
             A.decode_attn_v4_flash(self.q[l], self.cache[l, 0], self.cache[l, 1], self.out[l],
                                    self.H, self.HKV, self.D, kv, stream)
 
-    def run_group_e2e(self, A, kv: int, stream) -> None:
-        for l in range(self.L):
-            self.q[l].copy_(self.q_host[l], non_blocking=True)
-            A.decode_attn_v4_flash(self.q[l], self.cache[l, 0], self.cache[l, 1], self.out[l],
-                                   self.H, self.HKV, self.D, kv, stream)
-            self.out_host[l].copy_(self.out[l], non_blocking=True)
-
     def e2e_bytes(self):
         per = self.H * self.D * 2
         n = self.L * len(self.groups)
@@ -307,11 +300,6 @@ class Cfg3:
     def run_group(self, A, key, stream) -> None:
         A.decode_attn_batched(self.q, self.kpool, self.vpool, self.offs, self.lens, self.out,
                               self.U, self.G, 1, self.D, self.rows, self.max_len, stream)
-
-    def run_group_e2e(self, A, key, stream) -> None:
-        self.q.copy_(self.q_host, non_blocking=True)
-        self.run_group(A, key, stream)
-        self.out_host.copy_(self.out, non_blocking=True)
 
     def e2e_bytes(self):
         n = self.U * self.G * self.D * 2
@@ -468,11 +456,6 @@ class Cfg4:
             else:
                 self.dec(self.q[l], self.k[l], self.v[l], self.n, self.out[l], stream)
 
-    def run_group_e2e(self, A, key, stream) -> None:
-        self.q.copy_(self.q_host, non_blocking=True)
-        self.run_group(A, key, stream)
-        self.out_host.copy_(self.out, non_blocking=True)
-
     def e2e_bytes(self):
         n = self.L * self.H * self.D * 2
         return n, n
@@ -605,9 +588,20 @@ def run_ours(args, torch, dist, rank, local_rank, world):
         Ke = max(3, min(K, 200))
         ev2 = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in wl.groups]
                for _ in range(Ke)]
+        def e2e_group(kv):
+            # One decode step's worth of a group: the group's q (every layer)
+            # from pinned host memory, its calls (the same CUDA graph as the
+            # timed loop, or eager launches), its outputs back to pinned host.
+            wl.q.copy_(wl.q_host, non_blocking=True)
+            if use_graph:
+                graphs[kv].replay()
+            else:
+                wl.run_group(A, kv, stream)
+            wl.out_host.copy_(wl.out, non_blocking=True)
+
         with torch.cuda.stream(stream):
             for kv in wl.groups:
-                wl.run_group_e2e(A, kv, stream)
+                e2e_group(kv)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -618,7 +612,7 @@ def run_ours(args, torch, dist, rank, local_rank, world):
                     if align is not None:
                         dist.all_reduce(align)
                     ev2[k][i][0].record(stream)
-                    wl.run_group_e2e(A, kv, stream)
+                    e2e_group(kv)
                     ev2[k][i][1].record(stream)
         torch.cuda.synchronize()
         e_ms = sum(ev2[k][i][0].elapsed_time(ev2[k][i][1]) for k in range(Ke)
@@ -630,8 +624,10 @@ def run_ours(args, torch, dist, rank, local_rank, world):
         h2d, d2h = wl.e2e_bytes()
         e2e = {"value": job_bytes * Ke / (e_ms * 1e-3) / 1e9, "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "how": "per call: H2D q from pinned host, fr_decode_attn, D2H out to pinned host; "
-                      "eager launches, CUDA events, L2 flushed per kv_len group"}
+               "how": "per group of calls (one decode step's layers at one kv_len): one H2D of "
+                      "every layer's q from pinned host, the calls through the C ABI (CUDA "
+                      "graph unless --no-graph), one D2H of every output to pinned host; "
+                      "CUDA events around all three, L2 flushed before each group"}
 
     close = getattr(getattr(wl, "dec", None), "close", None)
     if close is not None:
