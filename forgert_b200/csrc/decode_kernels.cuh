@@ -167,9 +167,15 @@ struct SplitSmem {
     static constexpr int kSubBytes = TILE * 128;                   // one [TILE][64] box
     static constexpr int kTileBytes = kSub * kSubBytes;            // K (or V) of one stage
     static constexpr size_t kRingBytes = size_t(2) * STAGES * kTileBytes;
-    static constexpr size_t kBarOffset = kRingBytes;
+    static constexpr size_t kBarOffset = kRingBytes;                // full, empty, recv
+    // Cluster merge receive area (outside the ring: peers may push into it
+    // while this CTA still streams): CL messages of [m GP][l GP][acc slice],
+    // at most 2*GP*16 + GP*D floats for clusters of up to 16 CTAs.
+    static constexpr size_t kRecvOffset =
+        (kBarOffset + (2 * STAGES + 1) * sizeof(uint64_t) + 15) / 16 * 16;
+    static constexpr size_t kRecvFloats = size_t(2 * NT * 8 * 16 + NT * 8 * D + 64);
     // +1024: the ring is realigned to 1024 bytes (128-byte swizzle atom).
-    static constexpr size_t kBytes = 1024 + kRingBytes + 2 * STAGES * sizeof(uint64_t);
+    static constexpr size_t kBytes = 1024 + kRecvOffset + kRecvFloats * sizeof(float);
     // Cross-warp merge area (reuses the ring once every tile is consumed).
     static constexpr size_t kMergeBytes =
         size_t(NW) * (NT * 8) * D * sizeof(float) + size_t(NW) * (NT * 8) * 3 * sizeof(float);
@@ -229,6 +235,8 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     unsigned char* vring = smem + STAGES * S::kTileBytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
     uint64_t* empty = full + STAGES;
+    uint64_t* recv_bar = empty + STAGES;                                 // cluster merge pushes
+    float* recv = reinterpret_cast<float*>(smem + S::kRecvOffset);
     float* st_acc = reinterpret_cast<float*>(smem + S::kStateOffset);   // [GP][D]
     float* st_m = st_acc + GP * D;                                       // [GP]
     float* st_l = st_m + GP;                                             // [GP]
@@ -257,14 +265,26 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     // Every CTA of this grid is running: the next grid may start launching.
     grid_launch_dependents();
 
+    // Fused merge across a cluster: every CTA pushes each peer its (m, l) and
+    // that peer's slice of acc (st.async into the peer's receive area, bytes
+    // counted on the peer's recv_bar), so the merge needs no barrier after
+    // the loop; the cluster barrier armed here only guarantees that every
+    // CTA's recv_bar is initialised before anyone pushes.
+    const bool cluster_merge = CL > 1 && p.counters != nullptr;
+    const int x_nel = gcount * D;                    // merged elements of this unit
+    const int x_per = (x_nel + CL - 1) / CL;         // slice per cluster rank (a multiple of 4)
+    const int x_msg = 2 * GP + x_per;                // floats per message
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NW);
         }
+        mbar_init(recv_bar, 1);
+        if (cluster_merge) mbar_arrive_expect_tx(recv_bar, uint32_t(CL * x_msg * 4));
         fence_mbar_init();
     }
     __syncthreads();
+    if (cluster_merge) cluster_arrive_release();
 
     bool ok = true;
     const int g = lane >> 2;     // fragment row group
@@ -679,9 +699,30 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         }
     };
 
-    if constexpr (CL > 1) cluster_sync_all();       // every CTA's state is in its smem
+    if constexpr (CL > 1) {
+        // Push: message [m GP][l GP][acc slice j] to every cluster rank j,
+        // stored at [my rank] of its receive area.
+        cluster_wait_acquire();                      // every recv_bar is initialised
+        const int chunks = x_msg / 4;
+        const uint32_t recv_s = smem_u32(recv), bar_s = smem_u32(recv_bar);
+        for (int idx = threadIdx.x; idx < CL * chunks; idx += blockDim.x) {
+            const int j = idx / chunks;
+            const int f = (idx - j * chunks) * 4;    // first float of the chunk in the message
+            float4 v;
+            if (f < GP) {
+                v = *reinterpret_cast<const float4*>(st_m + f);
+            } else if (f < 2 * GP) {
+                v = *reinterpret_cast<const float4*>(st_l + (f - GP));
+            } else {
+                const int e = j * x_per + (f - 2 * GP);
+                v = e < x_nel ? *reinterpret_cast<const float4*>(st_acc + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            st_async_v4(dsmem_addr(recv_s + uint32_t(crank * x_msg + f) * 4u, uint32_t(j)), v,
+                        dsmem_addr(bar_s, uint32_t(j)));
+        }
+        if (!mbar_wait_bounded(recv_bar, 0)) record_error(p.err, kDevTimeoutFull);
+    }
     {
-        const uint32_t acc_s = smem_u32(st_acc), m_s = smem_u32(st_m), l_s = smem_u32(st_l);
         for (int e = e_begin + threadIdx.x; e < e_end; e += blockDim.x) {
             const int hj = e / D;
             const int d = e - hj * D;
@@ -689,9 +730,10 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
 #pragma unroll
             for (int j = 0; j < CL; ++j) {
                 if constexpr (CL > 1) {
-                    mj[j] = ld_dsmem_f32(dsmem_addr(m_s + hj * 4, j));
-                    lj[j] = ld_dsmem_f32(dsmem_addr(l_s + hj * 4, j));
-                    aj[j] = ld_dsmem_f32(dsmem_addr(acc_s + (hj * D + d) * 4, j));
+                    const float* msg = recv + j * x_msg;
+                    mj[j] = msg[hj];
+                    lj[j] = msg[GP + hj];
+                    aj[j] = msg[2 * GP + (e - e_begin)];
                 } else {
                     mj[j] = st_m[hj];
                     lj[j] = st_l[hj];
@@ -726,10 +768,6 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
             }
         }
     }
-    // This CTA's DSMEM reads are done; peers may retire once everyone arrives
-    // (the matching wait sits at the end, off the critical path).
-    if constexpr (CL > 1) cluster_arrive_release();
-
     if (ncl > 1) {
         __syncthreads();                             // slice stores of this CTA are done
         if (threadIdx.x == 0) {
@@ -831,7 +869,6 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         }
         if (!ok) record_error(p.err, kDevTimeoutPeer);
     }
-    if constexpr (CL > 1) cluster_wait_acquire();   // peers done reading this CTA's smem
     if (xmode) {
         // The last CTA of the grid to get here advances the epoch; every CTA
         // read it above (ordered before its count by the barrier and fence).

@@ -179,6 +179,16 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
     return v;
 }
 
+// 16-byte store into another CTA's shared memory (cluster address) that
+// completes 16 transaction bytes on that CTA's mbarrier (cluster address).
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float4 v, uint32_t mbar) {
+    asm volatile(
+        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+        :: "r"(addr), "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)),
+           "r"(__float_as_uint(v.z)), "r"(__float_as_uint(v.w)), "r"(mbar)
+        : "memory");
+}
+
 __device__ __forceinline__ void st_dsmem_u32(uint32_t addr, uint32_t v) {
     asm volatile("st.shared::cluster.u32 [%0], %1;" :: "r"(addr), "r"(v) : "memory");
 }
