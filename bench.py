@@ -235,7 +235,7 @@ class Cfg2:
         return {
             "workload": "cfg2: Qwen2-1.5B-shape decode attention, batch 1 per GPU, "
                         "28 layers x kv_len {512, 2048, 4096, 16384}",
-            "model": "Qwen2-1.5B attention shape (random data)",
+            "shape": "Qwen2-1.5B attention (H12, Hkv2, D128), random data",
             "batch_per_gpu": 1, "num_heads": self.H, "num_kv_heads": self.HKV,
             "head_dim": self.D, "layers": self.L, "kv_lens": self.groups,
             "cache": "contiguous fp16 [28 x 2 x 16384 x 2 x 128] per GPU",
@@ -309,7 +309,7 @@ class Cfg3:
         return {
             "workload": "cfg3: Qwen2-7B-shape batched decode attention, 64 sequences, ragged "
                         "kv_len U{1024..8192} (seed 2), sharded by (sequence, kv head)",
-            "model": "Qwen2-7B attention shape (random data)",
+            "shape": "Qwen2-7B attention (H28, Hkv4, D128), random data",
             "global_batch": 64, "num_heads": self.H, "num_kv_heads": self.HKV,
             "head_dim": self.D, "total_kv_tokens": int(self.lens_all.sum()),
             "units_this_rank": self.U,
@@ -468,7 +468,7 @@ class Cfg4:
             "exchange": {"none": "single GPU", "peer": "in-kernel peer stores over NVLink + "
                          "merge (fr_decode_attn_exchange)", "nccl": "NCCL all-gather + merge "
                          "kernel"}[self.exchange],
-            "model": "Qwen2-7B attention shape (random data)",
+            "shape": "Qwen2-7B attention (H28, Hkv4, D128), random data",
             "global_batch": 1, "num_heads": self.H, "num_kv_heads": self.HKV,
             "head_dim": self.D, "kv_len": self.T, "kv_rows_this_rank": self.n,
             "layers": self.L,
