@@ -764,8 +764,8 @@ def run_reference(args, rank, world):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp32 (fp16-valued inputs)", "data": "synthetic N(0,1) fp16",
         "impl": "reference",
-        "config": {"workload": "cfg2: Qwen2-1.5B-shape decode attention, batch 1, 28 layers x "
-                               "kv_len {512, 2048, 4096, 16384}",
+        "config": {"workload": "cfg2: Qwen2-1.5B-shape decode attention, batch 1 per GPU, 28 "
+                               "layers x kv_len {512, 2048, 4096, 16384}",
                    "num_heads": 12, "num_kv_heads": 2, "head_dim": 128, "layers": 28,
                    "kv_lens": list(W.CFG2_KV_LENS)},
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": runner.threads,
