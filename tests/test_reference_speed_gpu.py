@@ -202,3 +202,52 @@ def test_prologue_vs_reference_sequence(ref, H, Hkv, D):
         "fused_us": round(us_our, 2), "speedup": round(us_ref / us_our, 1),
         "bit_exact_fraction": round(exact / total, 6)}}))
     assert us_our < us_ref
+
+
+@pytest.mark.parametrize("H,Hkv,D,T", [(14, 2, 64, 512), (14, 2, 64, 2048), (28, 4, 128, 2048)])
+def test_prefill_vs_reference(ref, H, Hkv, D, T):
+    """Causal prefill over T positions: the reference's prefill_attn_causal
+    (kernels/attention_decode.cu:563-619, one thread per (head, position))
+    against fr_prefill_attn (the split kernel, one 'sequence' per query
+    position), each as a CUDA graph on the same buffers, 20 replays."""
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(T + D)
+    q = torch.from_numpy(W.normal_fp16(rng, (T, H, D))).to(dev)
+    k = torch.from_numpy(W.normal_fp16(rng, (T, Hkv, D))).to(dev)
+    v = torch.from_numpy(W.normal_fp16(rng, (T, Hkv, D))).to(dev)
+    out_ref = torch.empty_like(q)
+    out = torch.empty_like(q)
+    stream = torch.cuda.Stream(dev)
+    sp = stream.cuda_stream
+
+    def ref_call():
+        ref.ref_prefill_attn_causal(q.data_ptr(), k.data_ptr(), v.data_ptr(), out_ref.data_ptr(),
+                                    T, H, Hkv, D, sp)
+
+    def our_call():
+        A.prefill_attn_causal(q, k, v, out, T, H, Hkv, D, stream)
+
+    res = {}
+    for name, fn in (("ref", ref_call), ("ours", our_call)):
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize()
+        g = _graph(fn, stream)
+        with torch.cuda.stream(stream):
+            g.replay()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(20):
+                g.replay()
+            e1.record(stream)
+        e1.synchronize()
+        res[name] = e0.elapsed_time(e1) * 1e3 / 20
+    assert A.device_error() == 0
+    a, r = O.max_errors(out.float().cpu().numpy(), out_ref.float().cpu().numpy(), 1e-3)
+    assert a <= 2e-3 and r <= 1e-2, (a, r)
+    print("\n" + json.dumps({"prefill": {"shape": f"T{T} H{H} Hkv{Hkv} D{D}",
+                                         "ref_us": round(res["ref"], 1),
+                                         "ours_us": round(res["ours"], 1),
+                                         "speedup": round(res["ref"] / res["ours"], 1)}}))
+    assert res["ours"] < res["ref"]
