@@ -639,8 +639,14 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     for kv in wl.groups:
         us = group_ms[kv] * 1e3 / (K * wl.calls_per_group())
         gbs = wl.call_bytes(kv) / (us * 1e-6) / 1e9
+        i = wl.groups.index(kv)
+        per_step = np.array([ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(K)]) * 1e3 / \
+            wl.calls_per_group()
+        p10, p50, p90 = np.percentile(per_step, [10, 50, 90])
         sweep[str(kv)] = {"us_per_call": round(us, 3), "gbs": round(gbs, 1),
-                          "frac_of_measured_hbm": round(gbs / peak, 4)}
+                          "frac_of_measured_hbm": round(gbs / peak, 4),
+                          "us_per_call_p10_p50_p90": [round(float(p10), 3), round(float(p50), 3),
+                                                      round(float(p90), 3)]}
     dom = str(wl.groups[-1])
     tr = traffic_per_launch() if args.workload == "cfg2" else None
     roofline = {
