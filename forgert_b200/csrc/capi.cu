@@ -5,6 +5,7 @@
 // Declarations and contracts live in include/forgert_attn.h; each entry point
 // there names the reference launcher it replaces.
 #include "decode_kernels.cuh"
+#include "prefill_kernels.cuh"
 #include "rope_kernels.cuh"
 #include "../../include/forgert_attn.h"
 
@@ -533,6 +534,37 @@ int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* 
                                        state_ml, state_acc, mode, s, pdl);
 }
 
+// Causal prefill: grid (query tiles of 64, heads), programmatic dependent
+// launch on non-default streams.  The shared-memory attribute is set once per
+// device (bits 8/9 of attr_done).
+template <int D>
+int launch_prefill(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t s) {
+    constexpr int kStages = Stages<D>::value;
+    using PS = fr::PrefillSmem<D, kStages>;
+    auto fn = fr::prefill_kernel<D, kStages>;
+    const uint32_t bit = 1u << (D == 64 ? 8 : 9);
+    if (!(st->attr_done & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(PS::kBytes));
+        if (e != cudaSuccess) return cuda_fail(e);
+        st->attr_done |= bit;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((pp.T + PS::kTile - 1) / PS::kTile, pp.H, 1);
+    cfg.blockDim = dim3(160, 1, 1);
+    cfg.dynamicSmemBytes = PS::kBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = s != nullptr ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, pp);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
+
 DecodeParams base_params(const void* q, int num_heads, int num_kv_heads) {
     DecodeParams p;
     std::memset(&p, 0, sizeof(p));
@@ -820,16 +852,26 @@ int fr_prefill_attn(const void* q, const void* k, const void* v, void* out, int 
     if (!q || !k || !v || !out || seq_len <= 0) return FR_ERR_INVALID_ARG;
     int rc = check_heads(num_heads, num_kv_heads, head_dim);
     if (rc != FR_OK) return rc;
-    if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 4) || !aligned(out, 4))
+    if (!aligned(k, 16) || !aligned(v, 16) || !aligned(q, 16) || !aligned(out, 4))
         return FR_ERR_MISALIGNED;
-    // Query position s is a "sequence" of length s + 1 over the shared cache.
-    DecodeParams p = base_params(q, num_heads, num_kv_heads);
-    rc = encode_pair(&p, k, v, head_dim, num_kv_heads, seq_len);
+    DeviceState* st = nullptr;
+    rc = get_state(&st);
     if (rc != FR_OK) return rc;
-    p.causal = 1;
-    p.causal_offset = 0;
-    return run_decode(p, head_dim, seq_len, seq_len, static_cast<__half*>(out), nullptr, nullptr,
-                      4, static_cast<cudaStream_t>(stream));
+    fr::PrefillParams pp;
+    std::memset(&pp, 0, sizeof(pp));
+    rc = encode_kv_map(&pp.qmap, q, head_dim, num_heads, seq_len);
+    if (rc == FR_OK) rc = encode_kv_map(&pp.kmap, k, head_dim, num_kv_heads, seq_len);
+    if (rc == FR_OK) rc = encode_kv_map(&pp.vmap, v, head_dim, num_kv_heads, seq_len);
+    if (rc != FR_OK) return rc;
+    pp.out = static_cast<__half*>(out);
+    pp.T = seq_len;
+    pp.H = num_heads;
+    pp.Hkv = num_kv_heads;
+    pp.G = num_heads / num_kv_heads;
+    pp.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+    pp.err = st->err;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return head_dim == 64 ? launch_prefill<64>(st, pp, s) : launch_prefill<128>(st, pp, s);
 }
 
 int fr_reserve_workspace(size_t bytes) {

@@ -54,8 +54,6 @@ struct DecodeParams {
     const long long* row_offsets;// [B] first tensor-map row of each sequence, or nullptr (0)
     const int* kv_lens;          // [B] per-sequence lengths, or nullptr (use kv_len)
     int kv_len;
-    int causal;                  // 1: sequence b attends to positions [0, b + 1 + causal_offset)
-    int causal_offset;
     int zero_tail;               // 1: rows past a sequence's end may hold non-finite data
     int prefetch_rows;           // rows [0, prefetch_rows) may be loaded before the grid
                                  // dependency wait (they are not written by the preceding
@@ -256,7 +254,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     const int gcount = min(GP, p.G - hgrp * GP);
 
     // Sequence geometry.
-    const int seq_len = p.causal ? b + 1 + p.causal_offset : (p.kv_lens ? p.kv_lens[b] : p.kv_len);
+    const int seq_len = p.kv_lens ? p.kv_lens[b] : p.kv_len;
     const long long row_base = p.row_offsets ? p.row_offsets[b] : 0;
     const int pos_begin = split * p.split_len;
     const int pos_end = min(seq_len, pos_begin + p.split_len);

@@ -212,6 +212,21 @@ def test_prefill_golden_and_random():
     assert_close(out.cpu().numpy(), O.prefill_f64(q, k, v), what="prefill T300")
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("H,Hkv", [(14, 2), (28, 4), (8, 8), (32, 2)])
+@pytest.mark.parametrize("T", [1, 2, 63, 64, 65, 129, 700])
+def test_prefill_shapes_and_lengths(D, H, Hkv, T):
+    """Causal prefill across query-tile boundaries (64 rows), partial last
+    tiles and GQA groups of 1 to 16 heads."""
+    q, k, v = (W.normal_fp16(np.random.default_rng([T, H, Hkv, D, i]), (T, n, D))
+               for i, n in enumerate((H, Hkv, Hkv)))
+    out = nan_like(dev(q))
+    A.prefill_attn_causal(dev(q), dev(k), dev(v), out, T, H, Hkv, D)
+    torch.cuda.synchronize()
+    assert A.device_error() == 0
+    assert_close(out.cpu().numpy(), O.prefill_f64(q, k, v), what=f"prefill T{T} H{H} Hkv{Hkv} D{D}")
+
+
 def test_rope_append_matches_oracle():
     rng = np.random.default_rng(8)
     H, Hkv, D, S, pos = 12, 2, 128, 600, 511
