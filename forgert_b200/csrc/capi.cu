@@ -784,6 +784,8 @@ int fr_decode_attn_exchange(const void* q, const void* k_local, const void* v_lo
     p.xrank = rank;
     p.xworld = world;
     p.xrows = num_heads;
+    static const int wait_ms = std::min(60000, std::max(1, env_int("FORGERT_EXCHANGE_WAIT_MS", 1000)));
+    p.xwait_ms = wait_ms;
     return run_decode(p, head_dim, 1, std::max(1, local_kv_len), static_cast<__half*>(out),
                       nullptr, nullptr, 1, static_cast<cudaStream_t>(stream));
 }

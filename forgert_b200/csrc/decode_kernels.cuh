@@ -89,6 +89,7 @@ struct DecodeParams {
     void* xbuf[kMaxRanks];       // exchange buffer of each rank ([xrank] = this GPU's)
     int xrank, xworld;
     int xrows;                   // head rows per state (B * H)
+    int xwait_ms;                // longest wait for the other ranks' words (ms)
 };
 
 // Layout of one rank's exchange buffer (bytes from its base):
@@ -120,16 +121,17 @@ struct XLayout {
     }
 };
 
-// Waits (bounded) until the word at `addr` carries tag `epoch`; returns its
-// value.  `ok` is cleared on timeout, after which no further waits are made.
+// Waits (at most limit_ns) until the word at `addr` carries tag `epoch`;
+// returns its value.  `ok` is cleared on timeout, after which no further
+// waits are made.
 __device__ __forceinline__ float x_wait_word(const uint64_t* addr, uint64_t w, uint32_t epoch,
-                                             bool& ok) {
+                                             bool& ok, unsigned long long limit_ns) {
     if (uint32_t(w >> 32) != epoch && ok) {
         const unsigned long long t0 = globaltimer_ns();
         do {
             w = ld_relaxed_sys_u64(addr);
             if (uint32_t(w >> 32) == epoch) break;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 ok = false;
                 break;
             }
@@ -829,6 +831,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     // slice over the ranks.
     if (xmode && (ncl == 1 || st_flag[0])) {
         void* xb = p.xbuf[p.xrank];
+        const unsigned long long xlimit = 1000000ull * (unsigned long long)p.xwait_ms;
         bool ok = true;
         for (int e = e_begin + threadIdx.x; e < e_end; e += blockDim.x) {
             const int hj = e / D;
@@ -850,11 +853,11 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
             for (int j = 0; j < kMaxRanks; ++j) {
                 if (j < p.xworld) {
                     const uint64_t* mlp = XLayout::ml(xb, xpar, j, p.xworld, p.xrows) + 2 * hrow;
-                    const float mj = x_wait_word(mlp, wm[j], xepoch, ok);
-                    const float lj = x_wait_word(mlp + 1, wl[j], xepoch, ok);
+                    const float mj = x_wait_word(mlp, wm[j], xepoch, ok, xlimit);
+                    const float lj = x_wait_word(mlp + 1, wl[j], xepoch, ok, xlimit);
                     const float aj = x_wait_word(
                         XLayout::acc(xb, xpar, j, p.xworld, p.xrows, D) + hrow * D + d, wa[j],
-                        xepoch, ok);
+                        xepoch, ok, xlimit);
                     const float mn = fmaxf(m, mj);
                     const float mu = (mn == -INFINITY) ? 0.f : mn;
                     const float c_old = fast_exp2(m - mu), c_new = fast_exp2(mj - mu);

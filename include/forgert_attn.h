@@ -167,8 +167,8 @@ FR_API int fr_lse_merge_strided(const float* states_ml, const float* states_acc,
  * launched.  Each state word is stored with the call's sequence number in
  * one 8-byte access, so a receiver needs no fence or flag: it waits until the
  * words it reads carry its own call number.  If a peer does not take part,
- * the wait ends after about a second with FR_ERR_TIMEOUT from
- * fr_get_device_error; the exchange state is then inconsistent and every rank
+ * the wait ends after about a second (FORGERT_EXCHANGE_WAIT_MS, 1 to 60000,
+ * read once per process) with FR_ERR_TIMEOUT from fr_get_device_error; the exchange state is then inconsistent and every rank
  * must fr_exchange_reset its buffer (stream ordered) before the next call.
  *   q, out     [num_heads, head_dim] fp16 (the same q on every rank)
  *   k_local, v_local  this GPU's rows [local_kv_len, num_kv_heads, head_dim] */
