@@ -343,6 +343,13 @@ int max_cluster() {
     return v;
 }
 
+// CTA waves a batched or paged call plans for (ragged batches: several waves
+// of shorter splits balance the tail).
+int batch_waves() {
+    static const int v = std::min(16, std::max(2, env_int("FORGERT_BATCH_WAVES", 4)));
+    return v;
+}
+
 int one_cluster_tiles() {
     static const int v = env_int("FORGERT_ONE_CLUSTER_TILES", 4);
     return v;
@@ -622,9 +629,8 @@ int fr_decode_attn_batched(const void* q, const void* k_pool, const void* v_pool
     p.row_offsets = row_offsets;
     p.kv_lens = kv_lens;
     p.zero_tail = 1;
-    // Ragged batches: several waves of shorter splits balance the tail.
     return run_decode(p, head_dim, batch, std::max(1, max_kv_len), static_cast<__half*>(out),
-                      nullptr, nullptr, 4, static_cast<cudaStream_t>(stream));
+                      nullptr, nullptr, batch_waves(), static_cast<cudaStream_t>(stream));
 }
 
 int fr_decode_attn_paged(const void* q, const void* k_pages, const void* v_pages,
@@ -655,7 +661,7 @@ int fr_decode_attn_paged(const void* q, const void* k_pages, const void* v_pages
     p.kv_lens = kv_lens;
     p.zero_tail = 1;        // the last page's rows past the end may hold anything
     return run_decode(p, head_dim, batch, std::max(1, max_kv_len), static_cast<__half*>(out),
-                      nullptr, nullptr, 4, static_cast<cudaStream_t>(stream));
+                      nullptr, nullptr, batch_waves(), static_cast<cudaStream_t>(stream));
 }
 
 int fr_decode_attn_partial(const void* q, const void* k_cache, const void* v_cache, int kv_len,
