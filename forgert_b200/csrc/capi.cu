@@ -6,6 +6,7 @@
 // there names the reference launcher it replaces.
 #include "decode_kernels.cuh"
 #include "prefill_kernels.cuh"
+#include "prefill_tc_kernels.cuh"
 #include "rope_kernels.cuh"
 #include "../../include/forgert_attn.h"
 
@@ -572,6 +573,48 @@ int launch_prefill(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t s)
     return e == cudaSuccess ? FR_OK : cuda_fail(e);
 }
 
+// Causal prefill on tcgen05: grid (query tiles of 128, heads), 192 threads,
+// one CTA per SM (shared memory and the tensor-memory columns it allocates);
+// attribute bits 10/11 of attr_done.
+template <int D>
+int launch_prefill_tc(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t s) {
+    constexpr int kStages = D == 64 ? 4 : 3;
+    using PS = fr::PrefillTcSmem<D, kStages>;
+    auto fn = fr::prefill_tc_kernel<D, kStages>;
+    const uint32_t bit = 1u << (D == 64 ? 10 : 11);
+    if (!(st->attr_done & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(PS::kBytes));
+        if (e != cudaSuccess) return cuda_fail(e);
+        st->attr_done |= bit;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((pp.T + PS::kRows - 1) / PS::kRows, pp.H, 1);
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = PS::kBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = s != nullptr ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, pp);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
+
+// FORGERT_PREFILL_KERNEL selects the prefill kernel per call: "tc" (tcgen05)
+// or "mma" (mma.sync); unset means kPrefillDefaultTc.
+constexpr bool kPrefillDefaultTc = true;
+
+bool prefill_use_tc() {
+    const char* v = std::getenv("FORGERT_PREFILL_KERNEL");
+    if (v && std::strcmp(v, "tc") == 0) return true;
+    if (v && std::strcmp(v, "mma") == 0) return false;
+    return kPrefillDefaultTc;
+}
+
 DecodeParams base_params(const void* q, int num_heads, int num_kv_heads) {
     DecodeParams p;
     std::memset(&p, 0, sizeof(p));
@@ -879,6 +922,8 @@ int fr_prefill_attn(const void* q, const void* k, const void* v, void* out, int 
     pp.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
     pp.err = st->err;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (prefill_use_tc())
+        return head_dim == 64 ? launch_prefill_tc<64>(st, pp, s) : launch_prefill_tc<128>(st, pp, s);
     return head_dim == 64 ? launch_prefill<64>(st, pp, s) : launch_prefill<128>(st, pp, s);
 }
 
