@@ -574,12 +574,14 @@ int launch_prefill(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t s)
 }
 
 // Causal prefill on tcgen05: grid (query tiles of 128, heads), 192 threads,
-// one CTA per SM (shared memory and the tensor-memory columns it allocates);
-// attribute bits 10/11 of attr_done.
+// two CTAs per SM, each with 256 TMEM columns and at most half of the shared
+// memory (attribute bits 10/11 of attr_done).
 template <int D>
 int launch_prefill_tc(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t s) {
-    constexpr int kStages = D == 64 ? 4 : 3;
+    constexpr int kStages = D == 64 ? 4 : 2;
     using PS = fr::PrefillTcSmem<D, kStages>;
+    static_assert(2 * PS::kBytes <= 228 * 1024 && 3 * PS::kBytes > 228 * 1024,
+                  "exactly two CTAs per SM: their TMEM columns fill the SM");
     auto fn = fr::prefill_tc_kernel<D, kStages>;
     const uint32_t bit = 1u << (D == 64 ? 10 : 11);
     if (!(st->attr_done & bit)) {
@@ -604,15 +606,11 @@ int launch_prefill_tc(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t
     return e == cudaSuccess ? FR_OK : cuda_fail(e);
 }
 
-// FORGERT_PREFILL_KERNEL selects the prefill kernel per call: "tc" (tcgen05)
-// or "mma" (mma.sync); unset means kPrefillDefaultTc.
-constexpr bool kPrefillDefaultTc = true;
-
+// FORGERT_PREFILL_KERNEL selects the prefill kernel per call: "tc"
+// (tcgen05, the default) or "mma" (mma.sync).
 bool prefill_use_tc() {
     const char* v = std::getenv("FORGERT_PREFILL_KERNEL");
-    if (v && std::strcmp(v, "tc") == 0) return true;
-    if (v && std::strcmp(v, "mma") == 0) return false;
-    return kPrefillDefaultTc;
+    return !(v && std::strcmp(v, "mma") == 0);
 }
 
 DecodeParams base_params(const void* q, int num_heads, int num_kv_heads) {

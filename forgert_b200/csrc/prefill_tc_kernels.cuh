@@ -1,34 +1,39 @@
 // prefill_tc_kernels.cuh - causal prefill attention on the 5th-generation
-// tensor cores (tcgen05, accumulators in tensor memory).
+// tensor cores (tcgen05: MMAs issued by one thread, accumulators in tensor
+// memory).
 //
-// Same contract and result as prefill_kernel (prefill_kernels.cuh), which it
-// replaces as the default path of fr_prefill_attn: prefill_attn_causal
+// Same contract and result as prefill_kernel (prefill_kernels.cuh, the
+// mma.sync form kept as an alternative): prefill_attn_causal
 // (kernels/attention.cuh:76-82, kernels/attention_decode.cu:563-619), query
 // position s of head h attends to positions 0..s of kv head h / (H / Hkv),
 // scale 1/sqrt(D), fp32 softmax and accumulation, one fp16 rounding.
 //
-// One CTA per (128-row query tile, query head), 192 threads:
+// One CTA per (128-row query tile, query head), 192 threads, two CTAs per SM:
 //   warps 0-3  softmax: thread r owns query row r of the tile (TMEM lane r);
 //   warp 4     producer: TMA loads of the Q tile and of the causal K/V tiles
 //              (64 positions x D, 128-byte swizzle) through a STAGES ring;
 //   warp 5     allocates tensor memory; its lane 0 issues every tcgen05.mma.
+// Tensor memory (256 columns per CTA): S [0, 64), P_hi [64, 96), P_lo
+// [96, 128) (two fp16 per column), O [128, 128 + D).
 // Per K/V tile j:
-//   S_j = Q K_j^T            M=128, N=64, K=D; Q and K both K-major from the
-//                            TMA tiles; fp32 into TMEM columns [0, 64);
-//   softmax                  each thread reads its row of S_j (tcgen05.ld),
-//                            masks, updates the base-2 online softmax and
-//                            writes P_j as an fp16 pair (hi + lo, ~22 bits)
-//                            into shared memory in the 128-byte-swizzled
-//                            K-major layout of an MMA A operand;
-//   PV_j = P_j V_j           M=128, N=D, K=64 (hi and lo accumulate into the
-//                            same TMEM tile); V is the MN-major B operand read
-//                            straight from the TMA tile; two TMEM buffers
-//                            alternate so PV_j runs while the softmax warps
-//                            fold PV_{j-1} into their register accumulator:
-//                            O = (O + PV_{j-1}) * 2^(m_{j-1} - m_j).
-// The tensor pipe runs S_{j+1} as soon as the softmax warps have read S_j.
-// Every wait is bounded; on a timeout the kernel records an error, stops
-// issuing, waits for its own MMAs and copies and frees tensor memory.
+//   S_j = Q K_j^T          M=128, N=64, K=D; Q and K K-major from the TMA
+//                          tiles (shared-memory descriptors, 128B swizzle);
+//   softmax                each thread reads its row of S_j (tcgen05.ld),
+//                          masks the causal diagonal and rows past T, and
+//                          writes P_j = 2^(s - m_ref) as an fp16 pair
+//                          (hi + lo, ~22 significant bits) into tensor
+//                          memory (tcgen05.st);
+//   O += P_j V_j           M=128, N=D, K=64, A = P from tensor memory, B = V
+//                          MN-major straight from the TMA tile; hi and lo
+//                          accumulate into the same O.
+// m_ref is a per-row reference maximum that moves only when a row maximum
+// exceeds it by more than 2^8 (so P <= 256); the warp then rescales its rows
+// of O in tensor memory between PV_{j-1} and PV_j.  Any reference maximum
+// gives the same O / l.  The tensor pipe runs S_{j+1} as soon as the softmax
+// warps have read S_j; with two CTAs per SM one CTA's MMAs overlap the other
+// CTA's softmax.  Every wait is bounded: on a timeout the kernel records an
+// error, stops issuing, waits for its own MMAs and copies and frees tensor
+// memory.
 #pragma once
 #include "decode_kernels.cuh"
 #include "prefill_kernels.cuh"
@@ -38,30 +43,30 @@ namespace fr {
 
 template <int D, int STAGES>
 struct PrefillTcSmem {
-    static constexpr int kRows = 128;                       // query rows per CTA (MMA M)
-    static constexpr int kTile = 64;                        // K/V positions per tile (MMA N of S)
-    static constexpr int kSub = D / 64;                     // 128-byte column blocks of D
-    static constexpr int kQSubBytes = kRows * 128;          // [128 rows][64 dims]
+    static constexpr int kRows = 128;
+    static constexpr int kTile = 64;
+    static constexpr int kSub = D / 64;
+    static constexpr int kQSubBytes = kRows * 128;
     static constexpr int kQBytes = kSub * kQSubBytes;
-    static constexpr int kKvSubBytes = kTile * 128;         // [64 positions][64 dims]
+    static constexpr int kKvSubBytes = kTile * 128;
     static constexpr int kKvBytes = kSub * kKvSubBytes;
-    static constexpr int kPBytes = kRows * 128;             // [128 rows][64 positions] fp16
     static constexpr size_t kQOffset = 0;
     static constexpr size_t kKOffset = kQBytes;
     static constexpr size_t kVOffset = kKOffset + size_t(STAGES) * kKvBytes;
-    static constexpr size_t kPOffset = kVOffset + size_t(STAGES) * kKvBytes;  // hi, then lo
-    static constexpr size_t kBarOffset = kPOffset + 2 * size_t(kPBytes);
-    // barriers: q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full,
-    // s_free, p_full, pv_full[2], done; then the TMEM base address slot
-    static constexpr int kNumBars = 1 + 4 * STAGES + 6;
+    static constexpr size_t kBarOffset = kVOffset + size_t(STAGES) * kKvBytes;
+    // q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full, s_free,
+    // p_full, pv_full, done; then the TMEM base address slot
+    static constexpr int kNumBars = 1 + 4 * STAGES + 5;
     static constexpr size_t kBytes = 1024 + kBarOffset + kNumBars * sizeof(uint64_t) + 16;
-    // TMEM columns: S at [0, 64), PV buffer b at kPvCol + b * D
-    static constexpr uint32_t kPvCol = D >= 128 ? 128 : 64;
-    static constexpr uint32_t kTmemCols = (kPvCol + 2 * D) <= 256 ? 256 : 512;
+    static constexpr uint32_t kPhiCol = 64, kPloCol = 96, kOCol = 128;
+    static constexpr uint32_t kTmemCols = 256;
 };
 
+// Reference-maximum slack in log2 units: P = 2^(s - m_ref) <= 2^8.
+constexpr float kRescaleLog2 = 8.f;
+
 template <int D, int STAGES>
-__global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
+__global__ void __launch_bounds__(192, 2) prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
     using S = PrefillTcSmem<D, STAGES>;
     constexpr int ROWS = S::kRows;
     constexpr int TILE = S::kTile;
@@ -73,7 +78,6 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
     unsigned char* qs = smem + S::kQOffset;
     unsigned char* ks = smem + S::kKOffset;
     unsigned char* vs = smem + S::kVOffset;
-    unsigned char* ps = smem + S::kPOffset;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1;
@@ -83,8 +87,8 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
     uint64_t* s_full = v_empty + STAGES;
     uint64_t* s_free = s_full + 1;
     uint64_t* p_full = s_free + 1;
-    uint64_t* pv_full = p_full + 1;          // [2]
-    uint64_t* done = pv_full + 2;
+    uint64_t* pv_full = p_full + 1;
+    uint64_t* done = pv_full + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::kNumBars);
 
     const int nq = (p.T + ROWS - 1) / ROWS;
@@ -92,7 +96,7 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
     const int h = blockIdx.y;
     const int kvh = h / p.G;
     const int q0 = qt * ROWS;
-    const int nkv = (min(q0 + ROWS, p.T) + TILE - 1) / TILE;  // causal K/V tiles
+    const int nkv = (min(q0 + ROWS, p.T) + TILE - 1) / TILE;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
@@ -108,8 +112,7 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
         mbar_init(s_full, 1);
         mbar_init(s_free, 4);
         mbar_init(p_full, 4);
-        mbar_init(&pv_full[0], 1);
-        mbar_init(&pv_full[1], 1);
+        mbar_init(pv_full, 1);
         mbar_init(done, 1);
         fence_mbar_init();
     }
@@ -121,7 +124,7 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    grid_dependency_wait();                   // q, k, v may come from the preceding grid
+    grid_dependency_wait();
 
     if (warp == 4) {
         // ------------------------------------------------------ producer
@@ -151,7 +154,6 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
                     tma_load_4d(ks + s * S::kKvBytes + sub * S::kKvSubBytes, &p.kmap, 0, sub, kvh,
                                 j * TILE, &k_full[s], policy);
                 if (j >= STAGES && !mbar_wait_bounded(&v_empty[s], par)) {
-                    // K was issued: count this tile so its copy is drained
                     record_error(p.err, kDevTimeoutEmpty);
                     mbar_arrive_expect_tx(&v_full[s], 0);
                     ++issued;
@@ -164,7 +166,6 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
                                 j * TILE, &v_full[s], policy);
                 ++issued;
             }
-            // Drain: no copy in flight at exit.
             for (int j = max(0, issued - STAGES); j < issued; ++j) {
                 const uint32_t par = (j / STAGES) & 1;
                 if (!mbar_wait_bounded(&k_full[j % STAGES], par) ||
@@ -179,25 +180,22 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
         // ------------------------------------------------------ MMA issue
         if (lane == 0) {
             const uint32_t q_s = smem_u32(qs), k_s = smem_u32(ks), v_s = smem_u32(vs);
-            const uint32_t phi = smem_u32(ps), plo = phi + S::kPBytes;
-            const uint32_t t_s = tmem;
+            const uint32_t t_o = tmem + S::kOCol;
             bool ok = mbar_wait_bounded(q_full, 0);
-            // PV_i = P_i V_i into TMEM buffer i % 2 (hi then lo, same accumulator)
             auto issue_pv = [&](int i) -> bool {
                 const int s = i % STAGES;
                 if (!mbar_wait_bounded(&v_full[s], (i / STAGES) & 1) ||
                     !mbar_wait_bounded(p_full, i & 1))
                     return false;
                 tc_fence_after();
-                const uint32_t t_pv = tmem + S::kPvCol + uint32_t(i & 1) * D;
                 const uint32_t vt = v_s + s * S::kKvBytes;
 #pragma unroll
                 for (int kk = 0; kk < TILE / 16; ++kk) {
                     const uint64_t bd = umma_desc_sw128(vt + kk * 2048, S::kKvSubBytes, 1024);
-                    umma_f16(t_pv, umma_desc_sw128(phi + kk * 32, 16, 1024), bd, kIdescPV, kk > 0);
-                    umma_f16(t_pv, umma_desc_sw128(plo + kk * 32, 16, 1024), bd, kIdescPV, true);
+                    umma_f16_ts(t_o, tmem + S::kPhiCol + kk * 8, bd, kIdescPV, i > 0 || kk > 0);
+                    umma_f16_ts(t_o, tmem + S::kPloCol + kk * 8, bd, kIdescPV, true);
                 }
-                umma_commit(&pv_full[i & 1]);
+                umma_commit(pv_full);
                 umma_commit(&v_empty[s]);
                 return true;
             };
@@ -213,7 +211,7 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
 #pragma unroll
                 for (int kc = 0; kc < D / 16; ++kc) {
                     const int sub = kc / 4, c = kc % 4;
-                    umma_f16(t_s,
+                    umma_f16(tmem,
                              umma_desc_sw128(q_s + sub * S::kQSubBytes + c * 32, 16, 1024),
                              umma_desc_sw128(kt + sub * S::kKvSubBytes + c * 32, 16, 1024),
                              kIdescS, kc > 0);
@@ -224,24 +222,17 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
             }
             if (ok && !issue_pv(nkv - 1)) ok = false;
             if (!ok) record_error(p.err, kDevTimeoutFull);
-            // every MMA issued above has completed before tensor memory is freed
             umma_commit(done);
             if (!mbar_wait_bounded(done, 0)) record_error(p.err, kDevTimeoutFull);
         }
     } else {
         // --------------------------------------------------------- softmax
-        const int r = threadIdx.x;                       // tile row = TMEM lane
+        const int r = threadIdx.x;
         const int qrow = q0 + r;
         const uint32_t lane_base = uint32_t(warp * 32) << 16;
-        const uint32_t t_s = tmem + lane_base;
-        unsigned char* prow_hi = ps + r * 128;
-        unsigned char* prow_lo = prow_hi + S::kPBytes;
-        const int sw = r & 7;
+        const uint32_t t_row = tmem + lane_base;
         const float sl2 = p.scale_log2;
-        float o[D];
-#pragma unroll
-        for (int d = 0; d < D; ++d) o[d] = 0.f;
-        float m_run = -INFINITY, l_run = 0.f;
+        float m_ref = -INFINITY, l_run = 0.f;
         bool ok = true;
 
         for (int j = 0; j < nkv; ++j) {
@@ -251,7 +242,7 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
             }
             tc_fence_after();
             float sv[64];
-            tmem_ld64(t_s, sv);
+            tmem_ld64(t_row, sv);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(s_free);
@@ -265,90 +256,79 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
             float mx = -INFINITY;
 #pragma unroll
             for (int c = 0; c < TILE; ++c) mx = fmaxf(mx, sv[c]);
-            const float m_new = fmaxf(m_run, mx * sl2);
-            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-            const float alpha = fast_exp2(m_run - m_use);
-            m_run = m_new;
+            mx *= sl2;
+            float alpha = 1.f;
+            if (mx > m_ref + kRescaleLog2) {
+                alpha = fast_exp2(m_ref - mx);          // 0 on the first tile
+                m_ref = mx;
+            }
+            const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
             float rs = 0.f;
+            uint32_t hw[32], lw[32];
 #pragma unroll
-            for (int c = 0; c < TILE; ++c) {
-                sv[c] = fast_exp2(fmaf(sv[c], sl2, -m_use));
-                rs += sv[c];
+            for (int c = 0; c < 32; ++c) {
+                const float a = fast_exp2(fmaf(sv[2 * c], sl2, -m_use));
+                const float b = fast_exp2(fmaf(sv[2 * c + 1], sl2, -m_use));
+                rs += a + b;
+                const float ah = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+                const float bh = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
+                hw[c] = pack_half2(ah, bh);
+                lw[c] = pack_half2(a - ah, b - bh);
             }
             l_run = fmaf(l_run, alpha, rs);
 
-            // P_{j-1} is no longer read once PV_{j-1} has completed
-            if (j > 0 && !mbar_wait_bounded(&pv_full[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
-                ok = false;
-                break;
-            }
-            // P_j = hi + lo: hi keeps the top 11 significant bits (exact in
-            // fp16 for p >= 2^-14), lo the exact fp32 remainder.
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t hw[4], lw[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float a = sv[8 * c + 2 * e], b = sv[8 * c + 2 * e + 1];
-                    const float ah = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
-                    const float bh = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
-                    hw[e] = pack_half2(ah, bh);
-                    lw[e] = pack_half2(a - ah, b - bh);
+            if (j > 0) {
+                // PV_{j-1} complete: P may be overwritten and O is current
+                if (!mbar_wait_bounded(pv_full, (j - 1) & 1)) {
+                    ok = false;
+                    break;
                 }
-                const int off = ((c ^ sw) << 4);
-                *reinterpret_cast<uint4*>(prow_hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                *reinterpret_cast<uint4*>(prow_lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                    for (int c0 = 0; c0 < D; c0 += 32) {
+                        float ov[32];
+                        tmem_ld32(t_row + S::kOCol + c0, ov);
+                        uint32_t w[32];
+#pragma unroll
+                        for (int c = 0; c < 32; ++c) w[c] = __float_as_uint(ov[c] * alpha);
+                        tmem_st32(t_row + S::kOCol + c0, w);
+                    }
+                }
             }
-            fence_proxy_async_smem();
+            tmem_st32(t_row + S::kPhiCol, hw);
+            tmem_st32(t_row + S::kPloCol, lw);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
-
-            // O = (O + PV_{j-1}) * alpha while PV_j runs in the other buffer
-            if (j > 0) {
-                tc_fence_after();
-                const uint32_t t_pv = tmem + lane_base + S::kPvCol + uint32_t((j - 1) & 1) * D;
-#pragma unroll
-                for (int c0 = 0; c0 < D; c0 += 64) {
-                    float pv[64];
-                    tmem_ld64(t_pv + c0, pv);
-#pragma unroll
-                    for (int c = 0; c < 64; ++c) o[c0 + c] = (o[c0 + c] + pv[c]) * alpha;
-                }
-            }
         }
-        if (ok) {
-            const int last = nkv - 1;
-            if (!mbar_wait_bounded(&pv_full[last & 1], (last >> 1) & 1)) {
-                ok = false;
-            } else {
-                tc_fence_after();
-                const uint32_t t_pv = tmem + lane_base + S::kPvCol + uint32_t(last & 1) * D;
-#pragma unroll
-                for (int c0 = 0; c0 < D; c0 += 64) {
-                    float pv[64];
-                    tmem_ld64(t_pv + c0, pv);
-#pragma unroll
-                    for (int c = 0; c < 64; ++c) o[c0 + c] += pv[c];
-                }
-            }
-        }
+        if (ok && !mbar_wait_bounded(pv_full, (nkv - 1) & 1)) ok = false;
         if (!ok) record_error(p.err, kDevTimeoutFull);
-        if (ok && qrow < p.T) {
+        if (ok) {
+            tc_fence_after();
             const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
             __half* dst = p.out + ((size_t)qrow * p.H + h) * D;
-            if ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) {
+            const bool vec = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
 #pragma unroll
-                for (int d = 0; d < D; d += 8)
-                    *reinterpret_cast<uint4*>(dst + d) =
-                        make_uint4(pack_half2(o[d] * inv, o[d + 1] * inv),
-                                   pack_half2(o[d + 2] * inv, o[d + 3] * inv),
-                                   pack_half2(o[d + 4] * inv, o[d + 5] * inv),
-                                   pack_half2(o[d + 6] * inv, o[d + 7] * inv));
-            } else {
+            for (int c0 = 0; c0 < D; c0 += 64) {
+                float ov[64];
+                tmem_ld64(t_row + S::kOCol + c0, ov);   // whole warp, rows past T included
+                if (qrow < p.T) {
+                    if (vec) {
 #pragma unroll
-                for (int d = 0; d < D; d += 2)
-                    *reinterpret_cast<uint32_t*>(dst + d) = pack_half2(o[d] * inv, o[d + 1] * inv);
+                        for (int d = 0; d < 64; d += 8)
+                            *reinterpret_cast<uint4*>(dst + c0 + d) =
+                                make_uint4(pack_half2(ov[d] * inv, ov[d + 1] * inv),
+                                           pack_half2(ov[d + 2] * inv, ov[d + 3] * inv),
+                                           pack_half2(ov[d + 4] * inv, ov[d + 5] * inv),
+                                           pack_half2(ov[d + 6] * inv, ov[d + 7] * inv));
+                    } else {
+#pragma unroll
+                        for (int d = 0; d < 64; d += 2)
+                            *reinterpret_cast<uint32_t*>(dst + c0 + d) =
+                                pack_half2(ov[d] * inv, ov[d + 1] * inv);
+                    }
+                }
             }
         }
         tc_fence_before();

@@ -217,8 +217,9 @@ FR_API int fr_qkv_bias_rope_append(void* q, void* k, void* v, const void* q_bias
 
 /* Causal prefill attention: query position s attends to positions 0..s.
  * Replaces prefill_attn_causal (kernels/attention.cuh:76-82; definition
- * kernels/attention_decode.cu:563-619): a flash-attention kernel, one CTA per
- * (64 query positions, query head).
+ * kernels/attention_decode.cu:563-619): a flash-attention kernel on the
+ * tcgen05 tensor cores, one CTA per (128 query positions, query head)
+ * (FORGERT_PREFILL_KERNEL=mma selects the mma.sync form, 64 positions per CTA).
  *   q, out [seq_len, num_heads, head_dim]; k, v [seq_len, num_kv_heads, head_dim]
  * q, k, v 16-byte aligned (tensor-memory-access copies), out 4-byte aligned. */
 FR_API int fr_prefill_attn(const void* q, const void* k, const void* v, void* out, int seq_len,
