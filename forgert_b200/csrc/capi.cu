@@ -542,7 +542,7 @@ int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* 
                                        state_ml, state_acc, mode, s, pdl);
 }
 
-// Causal prefill: grid (query tiles of 64, heads), programmatic dependent
+// Causal prefill: grid (heads, query tiles of 64), programmatic dependent
 // launch on non-default streams.  The shared-memory attribute is set once per
 // device (bits 8/9 of attr_done).
 template <int D>
@@ -558,7 +558,7 @@ int launch_prefill(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t s)
         st->attr_done |= bit;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((pp.T + PS::kTile - 1) / PS::kTile, pp.H, 1);
+    cfg.gridDim = dim3(pp.H, (pp.T + PS::kTile - 1) / PS::kTile, 1);
     cfg.blockDim = dim3(160, 1, 1);
     cfg.dynamicSmemBytes = PS::kBytes;
     cfg.stream = s;
@@ -573,7 +573,7 @@ int launch_prefill(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t s)
     return e == cudaSuccess ? FR_OK : cuda_fail(e);
 }
 
-// Causal prefill on tcgen05: grid (query tiles of 128, heads), 192 threads,
+// Causal prefill on tcgen05: grid (heads, query tiles of 128), 192 threads,
 // two CTAs per SM, each with 256 TMEM columns and at most half of the shared
 // memory (attribute bits 10/11 of attr_done).
 template <int D>
@@ -591,7 +591,7 @@ int launch_prefill_tc(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t
         st->attr_done |= bit;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((pp.T + PS::kRows - 1) / PS::kRows, pp.H, 1);
+    cfg.gridDim = dim3(pp.H, (pp.T + PS::kRows - 1) / PS::kRows, 1);
     cfg.blockDim = dim3(192, 1, 1);
     cfg.dynamicSmemBytes = PS::kBytes;
     cfg.stream = s;

@@ -46,7 +46,7 @@ struct PrefillSmem {
     static constexpr size_t kBytes = 1024 + kBarOffset + (2 * STAGES + 1) * sizeof(uint64_t);
 };
 
-// grid = (ceil(T / 64) query tiles, H), block = 160 (4 consumer warps + producer).
+// grid = (H, ceil(T / 64) query tiles), block = 160 (4 consumer warps + producer).
 template <int D, int STAGES>
 __global__ void __launch_bounds__(160) prefill_kernel(const __grid_constant__ PrefillParams p) {
     using S = PrefillSmem<D, STAGES>;
@@ -66,8 +66,10 @@ __global__ void __launch_bounds__(160) prefill_kernel(const __grid_constant__ Pr
     uint64_t* qbar = empty + STAGES;
 
     const int nq = (p.T + TILE - 1) / TILE;
-    const int qt = nq - 1 - int(blockIdx.x);   // longest first
-    const int h = blockIdx.y;
+    // Heads vary fastest in launch order: every head's longest query tile
+    // is scheduled before any shorter one (longest-processing-time first).
+    const int h = blockIdx.x;
+    const int qt = nq - 1 - int(blockIdx.y);
     const int kvh = h / p.G;
     const int q0 = qt * TILE;
     const int nkv = qt + 1;                    // causal: K/V tiles 0..qt

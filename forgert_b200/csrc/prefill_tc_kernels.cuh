@@ -92,8 +92,10 @@ __global__ void __launch_bounds__(192, 2) prefill_tc_kernel(const __grid_constan
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::kNumBars);
 
     const int nq = (p.T + ROWS - 1) / ROWS;
-    const int qt = nq - 1 - int(blockIdx.x);  // longest first
-    const int h = blockIdx.y;
+    // Heads vary fastest in launch order: every head's longest query tile
+    // is scheduled before any shorter one (longest-processing-time first).
+    const int h = blockIdx.x;
+    const int qt = nq - 1 - int(blockIdx.y);
     const int kvh = h / p.G;
     const int q0 = qt * ROWS;
     const int nkv = (min(q0 + ROWS, p.T) + TILE - 1) / TILE;
