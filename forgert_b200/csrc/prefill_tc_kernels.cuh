@@ -255,9 +255,14 @@ __global__ void __launch_bounds__(192, 2) prefill_tc_kernel(const __grid_constan
                 for (int c = 0; c < TILE; ++c)
                     if (key0 + c > qrow || key0 + c >= p.T) sv[c] = -INFINITY;
             }
-            float mx = -INFINITY;
+            // 8 independent partial maxima / sums: short dependency chains
+            float pm[8];
 #pragma unroll
-            for (int c = 0; c < TILE; ++c) mx = fmaxf(mx, sv[c]);
+            for (int i = 0; i < 8; ++i) pm[i] = sv[i];
+#pragma unroll
+            for (int c = 8; c < TILE; ++c) pm[c & 7] = fmaxf(pm[c & 7], sv[c]);
+            float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
             mx *= sl2;
             float alpha = 1.f;
             if (mx > m_ref + kRescaleLog2) {
@@ -265,18 +270,19 @@ __global__ void __launch_bounds__(192, 2) prefill_tc_kernel(const __grid_constan
                 m_ref = mx;
             }
             const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-            float rs = 0.f;
+            float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             uint32_t hw[32], lw[32];
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
                 const float a = fast_exp2(fmaf(sv[2 * c], sl2, -m_use));
                 const float b = fast_exp2(fmaf(sv[2 * c + 1], sl2, -m_use));
-                rs += a + b;
+                ps[c & 7] += a + b;
                 const float ah = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
                 const float bh = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
                 hw[c] = pack_half2(ah, bh);
                 lw[c] = pack_half2(a - ah, b - bh);
             }
+            const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
             l_run = fmaf(l_run, alpha, rs);
 
             if (j > 0) {
