@@ -56,6 +56,7 @@ SIGNATURES = {
     "fr_version": (_i, []),
     "fr_launch_count": (ctypes.c_ulonglong, []),
     "fr_set_launch_overlap": (_i, [_i]),
+    "fr_copy_async": (_i, [_vp, _vp, ctypes.c_size_t, _vp]),
 }
 
 

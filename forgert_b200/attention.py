@@ -185,6 +185,21 @@ def decode_attn_exchange(q, k_local, v_local, local_kv_len: int, out, num_heads:
         _stream(stream)))
 
 
+def copy_async(dst, src, nbytes: int | None = None, stream=None) -> None:
+    """fr_copy_async: stream-ordered kernel copy; dst/src are CUDA tensors,
+    page-locked host tensors (``pin_memory()``) or raw pointers."""
+    def addr(x):
+        if isinstance(x, int):
+            return x
+        if not (x.is_cuda or x.is_pinned()):
+            raise ValueError("host tensors must be page-locked (pin_memory())")
+        return x.data_ptr()
+
+    if nbytes is None:
+        nbytes = min(dst.numel() * dst.element_size(), src.numel() * src.element_size())
+    check("fr_copy_async", load().fr_copy_async(addr(dst), addr(src), nbytes, _stream(stream)))
+
+
 def reserve_workspace(nbytes: int) -> None:
     lib = load()
     check("fr_reserve_workspace", lib.fr_reserve_workspace(nbytes))

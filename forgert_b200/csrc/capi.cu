@@ -8,6 +8,7 @@
 #include "prefill_kernels.cuh"
 #include "prefill_tc_kernels.cuh"
 #include "rope_kernels.cuh"
+#include "copy_kernels.cuh"
 #include "../../include/forgert_attn.h"
 
 #include <cuda.h>
@@ -991,6 +992,68 @@ const char* fr_status_string(int status) {
 int fr_version(void) { return kVersion; }
 
 int fr_set_launch_overlap(int enable) { return g_overlap.exchange(enable ? 1 : 0); }
+
+namespace {
+
+// Device-visible address of `p`: device or managed memory as is, page-locked
+// host memory through its mapping; nullptr for memory the device cannot reach
+// (pageable host memory).
+const void* device_view(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    switch (a.type) {
+        case cudaMemoryTypeDevice:
+        case cudaMemoryTypeManaged:
+            return p;
+        case cudaMemoryTypeHost:
+            return a.devicePointer;
+        default:
+            return nullptr;
+    }
+}
+
+}  // namespace
+
+int fr_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
+    if (bytes == 0) return FR_OK;
+    if (!dst || !src) return FR_ERR_INVALID_ARG;
+    const void* s = device_view(src);
+    void* d = const_cast<void*>(device_view(dst));
+    if (!s || !d) return FR_ERR_INVALID_ARG;
+    const bool vec = aligned(s, 16) && aligned(d, 16);
+    const size_t units = vec ? bytes / 16 : bytes;
+    const size_t per_cta = (size_t)fr::kCopyThreads * fr::kCopyUnroll;
+    int sms = 148;
+    {
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess)
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const size_t ctas = std::max<size_t>(1, std::min<size_t>(2 * (size_t)sms,
+                                                             (units + per_cta - 1) / per_cta));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ctas, 1, 1);
+    cfg.blockDim = dim3(fr::kCopyThreads, 1, 1);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = stream != nullptr ? 1 : 0;
+    cudaError_t e;
+    if (vec)
+        e = cudaLaunchKernelEx(&cfg, fr::copy_kernel, static_cast<const uint4*>(s),
+                               static_cast<uint4*>(d), units, (int)(bytes % 16));
+    else
+        e = cudaLaunchKernelEx(&cfg, fr::copy_bytes_kernel, static_cast<const unsigned char*>(s),
+                               static_cast<unsigned char*>(d), units);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
 
 unsigned long long fr_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 

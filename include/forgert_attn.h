@@ -252,6 +252,18 @@ FR_API int fr_version(void);
  * previous setting.  No reference counterpart. */
 FR_API int fr_set_launch_overlap(int enable);
 
+/* Stream-ordered copy of `bytes` from src to dst by a kernel.  Each pointer
+ * may be device memory or page-locked host memory (cudaHostAlloc,
+ * cudaMallocHost, cudaHostRegister), which the kernel reaches through its
+ * device mapping; pageable host memory gives FR_ERR_INVALID_ARG.  For the
+ * small per-step transfers of a decode step (a layer's q, token ids, an
+ * argmax result; the reference's runtime/executor.cpp:288-311 uses
+ * cudaMemcpy for these): it avoids the copy engine's fixed cost (~10 us per
+ * copy on B200), is graph-capturable and takes part in programmatic
+ * dependent launch like the attention calls.  16-byte aligned pointers copy
+ * by 16-byte vectors.  No reference counterpart. */
+FR_API int fr_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
 /* Number of kernels this library has launched (or recorded into a CUDA graph
  * under capture) in this process.  Diagnostics only; no reference
  * counterpart. */
