@@ -50,6 +50,7 @@ SIGNATURES = {
     "fr_decode_attn_exchange": (_i, [_vp, _vp, _vp, _i, _vp, _i, _i, _i,
                                      ctypes.POINTER(ctypes.c_void_p), _i, _i, _vp]),
     "fr_decode_workspace_size": (ctypes.c_size_t, [_i, _i, _i, _i, _i]),
+    "fr_prefill_workspace_size": (ctypes.c_size_t, [_i, _i, _i]),
     "fr_get_device_error": (_i, [_i, ctypes.POINTER(_i)]),
     "fr_last_cuda_error": (_i, []),
     "fr_status_string": (ctypes.c_char_p, [_i]),

@@ -205,6 +205,10 @@ def reserve_workspace(nbytes: int) -> None:
     check("fr_reserve_workspace", lib.fr_reserve_workspace(nbytes))
 
 
+def prefill_workspace_size(seq_len: int, num_heads: int, head_dim: int) -> int:
+    return int(load().fr_prefill_workspace_size(seq_len, num_heads, head_dim))
+
+
 def decode_workspace_size(batch: int, num_heads: int, num_kv_heads: int, head_dim: int,
                           max_kv_len: int) -> int:
     return int(load().fr_decode_workspace_size(batch, num_heads, num_kv_heads, head_dim,

@@ -574,11 +574,95 @@ int launch_prefill(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t s)
     return e == cudaSuccess ? FR_OK : cuda_fail(e);
 }
 
-// Causal prefill on tcgen05: grid (heads, query tiles of 128), 192 threads,
-// two CTAs per SM, each with 256 TMEM columns and at most half of the shared
-// memory (attribute bits 10/11 of attr_done).
+// Split plan of the tcgen05 prefill: K/V tiles per work unit (0 = one unit
+// per query tile), units and partial slots per head.  Causal query tiles
+// differ in length (the last has the most K/V tiles); when the longest one
+// outlasts the average load of a CTA slot (two per SM), the K/V ranges are
+// cut into units of half or a quarter of the longest range, merged by the
+// last unit of a query tile to finish.  The choice minimises the estimated
+// makespan max(longest unit, total work / slots), counting a fixed cost of
+// four tile times per unit and a merge of one tile time per unit of the
+// query tile for split units (fitted to B200 measurements of T 512..8192,
+// H 4..28); each finer split must gain 15 % on the estimate.
+// FORGERT_PREFILL_CHUNK forces the size (0 = never split), read per call.
+struct PrefillPlan {
+    int chunk_tiles = 0;
+    int units_per_head = 0;
+    int slots_per_head = 0;
+};
+
+PrefillPlan prefill_plan(int T, int H, int sm_count) {
+    constexpr int kRows = 128, kTile = 64;
+    constexpr double kFixed = 4.0, kMerge = 2.0;     // in K/V tile times
+    const int nq = (T + kRows - 1) / kRows;
+    auto tiles = [&](int qt) { return (std::min(qt * kRows + kRows, T) + kTile - 1) / kTile; };
+    const int nmax = tiles(nq - 1);
+    const double slots = 2.0 * sm_count;
+    // estimated makespan of chunk size ct (ct >= nmax: unsplit)
+    auto estimate = [&](int ct) {
+        double longest = 0, total = 0;
+        for (int qt = 0; qt < nq; ++qt) {
+            const int n = tiles(qt);
+            if (ct >= n) {
+                longest = std::max(longest, n + kFixed);
+                total += n + kFixed;
+            } else {
+                const int nc = (n + ct - 1) / ct;
+                for (int j = 0; j < n; j += ct) {
+                    const double w = std::min(ct, n - j) + kFixed + kMerge * nc / 2;
+                    longest = std::max(longest, w);
+                    total += w;
+                }
+            }
+        }
+        return std::max(longest, total * H / slots);
+    };
+    PrefillPlan pl;
+    pl.units_per_head = nq;
+    const int lo = std::max(1, (nmax + fr::kMaxPrefillChunks - 1) / fr::kMaxPrefillChunks);
+    int ct = 0;
+    const int forced = env_int("FORGERT_PREFILL_CHUNK", -1);
+    if (forced >= 0) {
+        ct = forced > 0 ? std::max(forced, lo) : 0;
+    } else if ((long long)H * nq <= kMaxUnits) {
+        const double base = estimate(nmax);
+        // When the total work per slot bounds the estimate, splitting only
+        // adds merges: search only when the longest query tile bounds it.
+        if (base <= nmax + kFixed) {
+            double best = base;
+            for (int parts = 2; parts <= fr::kMaxPrefillChunks; parts *= 2) {
+                const int c = (nmax + parts - 1) / parts;
+                if (c >= nmax) continue;
+                const double e = estimate(c);
+                if (e < 0.85 * best) {       // each finer split must gain 15 %
+                    best = e;
+                    ct = c;
+                }
+            }
+        }
+    }
+    if (ct <= 0 || ct >= nmax || (long long)H * nq > kMaxUnits) return pl;
+    pl.chunk_tiles = ct;
+    pl.units_per_head = 0;
+    for (int qt = 0; qt < nq; ++qt) {
+        const int nc = (tiles(qt) + ct - 1) / ct;
+        pl.units_per_head += nc;
+        if (nc > 1) pl.slots_per_head += nc;
+    }
+    return pl;
+}
+
+size_t prefill_partial_bytes(const PrefillPlan& pl, int H, int D) {
+    return (size_t)H * pl.slots_per_head * 128 * (D + 2) * sizeof(float);
+}
+
+// Causal prefill on tcgen05: grid (heads, work units), 192 threads, two CTAs
+// per SM, each with 256 TMEM columns and at most half of the shared memory
+// (attribute bits 10/11 of attr_done).  A split plan needs workspace for the
+// partial states; inside a graph capture that cannot grow it, the call runs
+// unsplit instead.
 template <int D>
-int launch_prefill_tc(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t s) {
+int launch_prefill_tc(DeviceState* st, fr::PrefillParams pp, cudaStream_t s) {
     constexpr int kStages = D == 64 ? 4 : 2;
     using PS = fr::PrefillTcSmem<D, kStages>;
     static_assert(2 * PS::kBytes <= 228 * 1024 && 3 * PS::kBytes > 228 * 1024,
@@ -591,8 +675,27 @@ int launch_prefill_tc(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t
         if (e != cudaSuccess) return cuda_fail(e);
         st->attr_done |= bit;
     }
+    const int nq = (pp.T + PS::kRows - 1) / PS::kRows;
+    PrefillPlan pl = prefill_plan(pp.T, pp.H, st->sm_count);
+    if (pl.chunk_tiles > 0) {
+        int rc = ensure_workspace(st, kCounterBytes + prefill_partial_bytes(pl, pp.H, D), s);
+        if (rc == FR_ERR_WORKSPACE) {
+            pl = PrefillPlan();
+            pl.units_per_head = nq;
+        } else if (rc != FR_OK) {
+            return rc;
+        }
+    }
+    if (pl.chunk_tiles > 0) {
+        const size_t slots = (size_t)pp.H * pl.slots_per_head;
+        pp.chunk_tiles = pl.chunk_tiles;
+        pp.slots_per_head = pl.slots_per_head;
+        pp.counters = static_cast<int*>(st->ws);
+        pp.part_acc = reinterpret_cast<float*>(static_cast<char*>(st->ws) + kCounterBytes);
+        pp.part_ml = pp.part_acc + slots * 128 * D;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(pp.H, (pp.T + PS::kRows - 1) / PS::kRows, 1);
+    cfg.gridDim = dim3(pp.H, pl.units_per_head, 1);
     cfg.blockDim = dim3(192, 1, 1);
     cfg.dynamicSmemBytes = PS::kBytes;
     cfg.stream = s;
@@ -947,6 +1050,14 @@ size_t fr_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int 
         return 0;
     const int splits = std::max(pl1.num_splits, pl4.num_splits) + kClusterCtas;
     return kCounterBytes + partial_bytes((long long)batch * num_heads, splits, head_dim);
+}
+
+size_t fr_prefill_workspace_size(int seq_len, int num_heads, int head_dim) {
+    if (seq_len <= 0 || num_heads <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
+    DeviceState* st = nullptr;
+    if (get_state(&st) != FR_OK) return 0;
+    const PrefillPlan pl = prefill_plan(seq_len, num_heads, st->sm_count);
+    return pl.chunk_tiles > 0 ? kCounterBytes + prefill_partial_bytes(pl, num_heads, head_dim) : 0;
 }
 
 int fr_get_device_error(int clear, int* device_code) {

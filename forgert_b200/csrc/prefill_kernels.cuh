@@ -31,6 +31,16 @@ struct PrefillParams {
     int T, H, Hkv, G;            // positions, query heads, kv heads, H / Hkv
     float scale_log2;            // log2(e) / sqrt(D)
     int* err;                    // device error word
+    // Split K/V ranges (tcgen05 kernel only; chunk_tiles == 0: one CTA per
+    // query tile).  A query tile with more than chunk_tiles K/V tiles is
+    // covered by several CTAs; each stores its unnormalised (O, m, l) in
+    // slot h * slots_per_head + (the tile's first slot) + chunk, and the last
+    // to arrive (counters[h * nq + query tile]) merges them.
+    int chunk_tiles;
+    int slots_per_head;
+    float* part_acc;             // [slots][D][128 rows]
+    float* part_ml;              // [slots][128 rows][2]
+    int* counters;               // zero between calls
 };
 
 template <int D, int STAGES>

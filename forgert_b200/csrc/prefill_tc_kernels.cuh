@@ -65,6 +65,27 @@ struct PrefillTcSmem {
 // Reference-maximum slack in log2 units: P = 2^(s - m_ref) <= 2^8.
 constexpr float kRescaleLog2 = 8.f;
 
+// Most units one query tile's K/V range is split into.
+constexpr int kMaxPrefillChunks = 4;
+
+// 64 outputs of one row, scaled by inv, as fp16 (16-byte stores when the
+// output base is 16-byte aligned, 4-byte stores otherwise).
+__device__ __forceinline__ void store_row64(__half* dst, const float (&v)[64], float inv, bool vec) {
+    if (vec) {
+#pragma unroll
+        for (int d = 0; d < 64; d += 8)
+            *reinterpret_cast<uint4*>(dst + d) =
+                make_uint4(pack_half2(v[d] * inv, v[d + 1] * inv),
+                           pack_half2(v[d + 2] * inv, v[d + 3] * inv),
+                           pack_half2(v[d + 4] * inv, v[d + 5] * inv),
+                           pack_half2(v[d + 6] * inv, v[d + 7] * inv));
+    } else {
+#pragma unroll
+        for (int d = 0; d < 64; d += 2)
+            *reinterpret_cast<uint32_t*>(dst + d) = pack_half2(v[d] * inv, v[d + 1] * inv);
+    }
+}
+
 template <int D, int STAGES>
 __global__ void __launch_bounds__(192, 2) prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
     using S = PrefillTcSmem<D, STAGES>;
@@ -92,13 +113,24 @@ __global__ void __launch_bounds__(192, 2) prefill_tc_kernel(const __grid_constan
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::kNumBars);
 
     const int nq = (p.T + ROWS - 1) / ROWS;
-    // Heads vary fastest in launch order: every head's longest query tile
-    // is scheduled before any shorter one (longest-processing-time first).
+    // Heads vary fastest in launch order; work units run longest query tile
+    // first (longest-processing-time first).  Unit u of a head is chunk c of
+    // query tile qt, enumerating tiles from the last and chunks in order.
     const int h = blockIdx.x;
-    const int qt = nq - 1 - int(blockIdx.y);
+    int qt = nq - 1, c = int(blockIdx.y), nc = 1, slot0 = 0;
+    const int ct = p.chunk_tiles;
+    for (;; --qt) {
+        const int n = (min(qt * ROWS + ROWS, p.T) + TILE - 1) / TILE;
+        nc = ct > 0 ? (n + ct - 1) / ct : 1;
+        if (c < nc || qt == 0) break;
+        c -= nc;
+        if (nc > 1) slot0 += nc;
+    }
     const int kvh = h / p.G;
     const int q0 = qt * ROWS;
-    const int nkv = (min(q0 + ROWS, p.T) + TILE - 1) / TILE;
+    const int nkv_all = (min(q0 + ROWS, p.T) + TILE - 1) / TILE;
+    const int j0 = nc > 1 ? c * ct : 0;                      // this unit's K/V tiles
+    const int nkv = nc > 1 ? min(ct, nkv_all - j0) : nkv_all;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
@@ -154,7 +186,7 @@ __global__ void __launch_bounds__(192, 2) prefill_tc_kernel(const __grid_constan
 #pragma unroll
                 for (int sub = 0; sub < S::kSub; ++sub)
                     tma_load_4d(ks + s * S::kKvBytes + sub * S::kKvSubBytes, &p.kmap, 0, sub, kvh,
-                                j * TILE, &k_full[s], policy);
+                                (j0 + j) * TILE, &k_full[s], policy);
                 if (j >= STAGES && !mbar_wait_bounded(&v_empty[s], par)) {
                     record_error(p.err, kDevTimeoutEmpty);
                     mbar_arrive_expect_tx(&v_full[s], 0);
@@ -165,7 +197,7 @@ __global__ void __launch_bounds__(192, 2) prefill_tc_kernel(const __grid_constan
 #pragma unroll
                 for (int sub = 0; sub < S::kSub; ++sub)
                     tma_load_4d(vs + s * S::kKvBytes + sub * S::kKvSubBytes, &p.vmap, 0, sub, kvh,
-                                j * TILE, &v_full[s], policy);
+                                (j0 + j) * TILE, &v_full[s], policy);
                 ++issued;
             }
             for (int j = max(0, issued - STAGES); j < issued; ++j) {
@@ -249,7 +281,7 @@ __global__ void __launch_bounds__(192, 2) prefill_tc_kernel(const __grid_constan
             __syncwarp();
             if (lane == 0) mbar_arrive(s_free);
 
-            const int key0 = j * TILE;
+            const int key0 = (j0 + j) * TILE;
             if (key0 + TILE - 1 > q0 || key0 + TILE > p.T) {
 #pragma unroll
                 for (int c = 0; c < TILE; ++c)
@@ -312,32 +344,89 @@ __global__ void __launch_bounds__(192, 2) prefill_tc_kernel(const __grid_constan
         }
         if (ok && !mbar_wait_bounded(pv_full, (nkv - 1) & 1)) ok = false;
         if (!ok) record_error(p.err, kDevTimeoutFull);
-        if (ok) {
+        __half* dst = p.out + ((size_t)qrow * p.H + h) * D;
+        const bool vec = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+        if (ok && nc == 1) {
             tc_fence_after();
             const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-            __half* dst = p.out + ((size_t)qrow * p.H + h) * D;
-            const bool vec = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
 #pragma unroll
             for (int c0 = 0; c0 < D; c0 += 64) {
                 float ov[64];
                 tmem_ld64(t_row + S::kOCol + c0, ov);   // whole warp, rows past T included
-                if (qrow < p.T) {
-                    if (vec) {
+                if (qrow < p.T) store_row64(dst + c0, ov, inv, vec);
+            }
+        } else if (nc > 1) {
+            // Split K/V range: store this unit's unnormalised row state
+            // (O d-major, [d][row], so a warp's stores and loads are whole
+            // 128-byte lines); the last unit of the query tile to arrive
+            // merges the others into its own state, read back from TMEM.
+            const size_t slot0g = (size_t)h * p.slots_per_head + slot0;
+            float2* mlp = reinterpret_cast<float2*>(p.part_ml) + slot0g * ROWS + r;
+            if (ok) {
+                tc_fence_after();
+                float* pa = p.part_acc + (slot0g + c) * ROWS * D + r;
 #pragma unroll
-                        for (int d = 0; d < 64; d += 8)
-                            *reinterpret_cast<uint4*>(dst + c0 + d) =
-                                make_uint4(pack_half2(ov[d] * inv, ov[d + 1] * inv),
-                                           pack_half2(ov[d + 2] * inv, ov[d + 3] * inv),
-                                           pack_half2(ov[d + 4] * inv, ov[d + 5] * inv),
-                                           pack_half2(ov[d + 6] * inv, ov[d + 7] * inv));
-                    } else {
+                for (int c0 = 0; c0 < D; c0 += 64) {
+                    float ov[64];
+                    tmem_ld64(t_row + S::kOCol + c0, ov);
 #pragma unroll
-                        for (int d = 0; d < 64; d += 2)
-                            *reinterpret_cast<uint32_t*>(dst + c0 + d) =
-                                pack_half2(ov[d] * inv, ov[d + 1] * inv);
+                    for (int d = 0; d < 64; ++d) pa[(c0 + d) * ROWS] = ov[d];
+                }
+                mlp[c * ROWS] = make_float2(m_ref, l_run);
+            }
+            uint32_t* last = tmem_slot + 1;
+            consumer_sync(4 * 32);                   // this unit's stores are done
+            if (threadIdx.x == 0) {
+                // acq_rel: publishes this unit's state and, for the last
+                // arriver, acquires the other units' states.
+                const int old = atom_add_acq_rel_gpu(&p.counters[h * nq + qt], 1);
+                *last = (old == nc - 1) ? 1u : 0u;
+            }
+            consumer_sync(4 * 32);
+            if (*last && ok) {
+                // O = sum_u O_u 2^(m_u - M) / sum_u l_u 2^(m_u - M), M = max_u m_u
+                float mu_[kMaxPrefillChunks], lu_[kMaxPrefillChunks];
+                float mmax = m_ref;
+#pragma unroll
+                for (int u = 0; u < kMaxPrefillChunks; ++u) {
+                    mu_[u] = -INFINITY;
+                    lu_[u] = 0.f;
+                    if (u < nc && u != c) {
+                        const float2 v = __ldcg(mlp + u * ROWS);
+                        mu_[u] = v.x;
+                        lu_[u] = v.y;
                     }
+                    mmax = fmaxf(mmax, mu_[u]);
+                }
+                const float msafe = mmax == -INFINITY ? 0.f : mmax;
+                const float w_own = fast_exp2(m_ref - msafe);
+                float lsum = l_run * w_own;
+#pragma unroll
+                for (int u = 0; u < kMaxPrefillChunks; ++u) {
+                    mu_[u] = fast_exp2(mu_[u] - msafe);          // weight (0 for absent units)
+                    lsum = fmaf(lu_[u], mu_[u], lsum);
+                }
+                const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+                tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < D; c0 += 64) {
+                    float ov[64];
+                    tmem_ld64(t_row + S::kOCol + c0, ov);        // whole warp
+#pragma unroll
+                    for (int d = 0; d < 64; ++d) ov[d] *= w_own;
+#pragma unroll
+                    for (int u = 0; u < kMaxPrefillChunks; ++u) {
+                        if (u < nc && u != c) {
+                            const float* src = p.part_acc + ((slot0g + u) * D + c0) * ROWS + r;
+#pragma unroll
+                            for (int d = 0; d < 64; ++d)
+                                ov[d] = fmaf(__ldcg(src + d * ROWS), mu_[u], ov[d]);
+                        }
+                    }
+                    if (qrow < p.T) store_row64(dst + c0, ov, inv, vec);
                 }
             }
+            if (*last && threadIdx.x == 0) p.counters[h * nq + qt] = 0;   // ready for the next call
         }
         tc_fence_before();
     }

@@ -231,6 +231,13 @@ FR_API int fr_prefill_attn(const void* q, const void* k, const void* v, void* ou
 FR_API int fr_reserve_workspace(size_t bytes);
 FR_API size_t fr_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
                                 int max_kv_len);
+/* Workspace bytes fr_prefill_attn uses for seq_len positions and num_heads
+ * query heads (0 when the call needs none).  Prefill splits the K/V range
+ * of long query tiles over several CTAs when the grid would otherwise leave
+ * SMs idle; inside a CUDA-graph capture whose workspace is too small it runs
+ * unsplit (same result, fewer CTAs), so reserve this much with
+ * fr_reserve_workspace() before capturing a prefill. */
+FR_API size_t fr_prefill_workspace_size(int seq_len, int num_heads, int head_dim);
 
 /* Reads (and optionally clears) the current device's in-kernel error word:
  * 0 = none, otherwise a bounded wait ran out (FR_ERR_TIMEOUT is returned by

@@ -88,6 +88,68 @@ def test_prefill_long_and_large_logits(kernel):
                  what=f"prefill long ({kernel})")
 
 
+@pytest.mark.parametrize("chunk", [0, 1, 2, 3, 7])
+@pytest.mark.parametrize("T,H,Hkv,D", [(700, 14, 2, 64), (1000, 12, 2, 128), (2048, 4, 1, 128)])
+def test_prefill_split_chunks(monkeypatch, chunk, T, H, Hkv, D):
+    """K/V ranges of long query tiles split into units of `chunk` tiles (0 =
+    unsplit; at most 4 units per query tile, so small chunks grow), merged
+    by the last unit to arrive; run twice to check the counters reset."""
+    monkeypatch.setenv("FORGERT_PREFILL_KERNEL", "tc")
+    monkeypatch.setenv("FORGERT_PREFILL_CHUNK", str(chunk))
+    q, k, v = (W.normal_fp16(np.random.default_rng([T, H, D, i, 11]), (T, n, D))
+               for i, n in enumerate((H, Hkv, Hkv)))
+    exact = O.prefill_f64(q, k, v)
+    for rep in range(2):
+        assert_close(run(q, k, v, T, H, Hkv, D), exact, what=f"split {chunk} rep {rep}")
+
+
+def test_prefill_workspace_and_graph_capture(monkeypatch):
+    """A split prefill inside a CUDA graph: with the workspace reserved
+    first it keeps its split plan; a shape needing more than the reservation
+    runs unsplit in the capture unless earlier calls grew the workspace
+    further; every form is exact."""
+    monkeypatch.setenv("FORGERT_PREFILL_KERNEL", "tc")
+    monkeypatch.delenv("FORGERT_PREFILL_CHUNK", raising=False)
+    assert A.prefill_workspace_size(8192, 28, 128) == 0            # fills the GPU unsplit
+    T, H, Hkv, D = 1500, 14, 2, 64
+    need = A.prefill_workspace_size(T, H, D)
+    assert need > 0
+    A.reserve_workspace(need)
+    q, k, v = (W.normal_fp16(np.random.default_rng([T, i, 12]), (T, n, D))
+               for i, n in enumerate((H, Hkv, Hkv)))
+    exact = O.prefill_f64(q, k, v)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    out = nan_like(qd)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        A.prefill_attn_causal(qd, kd, vd, out, T, H, Hkv, D, s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        A.prefill_attn_causal(qd, kd, vd, out, T, H, Hkv, D, torch.cuda.current_stream())
+    for _ in range(3):
+        out.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        assert A.device_error() == 0
+        assert_close(out.cpu().numpy(), exact, what="captured split prefill")
+    # a shape whose split plan needs more workspace than exists: unsplit in capture
+    T2, H2, Hkv2, D2 = 2048, 12, 2, 128
+    q2, k2, v2 = (W.normal_fp16(np.random.default_rng([T2, i, 13]), (T2, n, D2))
+                  for i, n in enumerate((H2, Hkv2, Hkv2)))
+    assert A.prefill_workspace_size(T2, H2, D2) > need
+    out2 = nan_like(dev(q2))
+    q2d, k2d, v2d = dev(q2), dev(k2), dev(v2)
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=s):
+        A.prefill_attn_causal(q2d, k2d, v2d, out2, T2, H2, Hkv2, D2, torch.cuda.current_stream())
+    g2.replay()
+    torch.cuda.synchronize()
+    assert A.device_error() == 0
+    assert_close(out2.cpu().numpy(), O.prefill_f64(q2, k2, v2), what="capture fallback")
+    del g, g2
+
+
 def test_prefill_kernels_timed(monkeypatch):
     """Both kernels on T = 2048 and 8192, H28 Hkv4 D128 (CUDA events, 10
     launches after 3 warm-ups).  Useful causal flops = 2 * 2 * H * D * T(T+1)/2."""
