@@ -17,9 +17,9 @@
  * Pointers are caller-owned device memory.  k/v bases must be 16-byte aligned
  * (tiles are moved with TMA tensor copies); q/out 4-byte aligned.
  *
- * Workspace: calls that split the KV range keep per-split (m, l, acc) partial
- * states in a library-owned per-device buffer that grows on demand with
- * cudaMalloc.  Growth cannot happen inside CUDA-graph capture, so size it with
+ * Workspace: calls that split the KV range (decode; prefill of short or
+ * few-head prompts) keep per-split (m, l, acc) partial states in a
+ * library-owned per-device buffer that grows on demand with cudaMalloc.  Growth cannot happen inside CUDA-graph capture, so size it with
  * fr_reserve_workspace() before capturing; a capture that would need more
  * returns FR_ERR_WORKSPACE.  The buffer is shared by all calls on a device:
  * calls on different streams of one device must not overlap in time.
