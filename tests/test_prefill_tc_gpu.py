@@ -182,3 +182,20 @@ def test_prefill_kernels_timed(monkeypatch):
             a, r = O.max_errors(outs[KERNELS[0]], outs[name], 1e-3)
             assert a <= 2e-3, (T, name, a, r)
     print("\n" + json.dumps({"prefill_kernels": res}))
+
+
+@pytest.mark.parametrize("kernel", KERNELS, indirect=True)
+@pytest.mark.parametrize("T,H,Hkv,D", [(300, 8, 2, 128), (2048, 4, 1, 64)])
+def test_prefill_output_4_byte_aligned(kernel, T, H, Hkv, D):
+    """out 4-byte but not 16-byte aligned (the C ABI's minimum): the kernels
+    store with 4-byte writes, unsplit and through the split merge."""
+    q, k, v = (W.normal_fp16(np.random.default_rng([T, D, i, 14]), (T, n, D))
+               for i, n in enumerate((H, Hkv, Hkv)))
+    buf = torch.full((T * H * D + 8,), float("nan"), dtype=torch.float16, device="cuda")
+    out = buf[2:2 + T * H * D].view(T, H, D)           # base + 4 bytes
+    assert out.data_ptr() % 16 == 4
+    A.prefill_attn_causal(dev(q), dev(k), dev(v), out, T, H, Hkv, D)
+    torch.cuda.synchronize()
+    assert A.device_error() == 0
+    assert_close(out.cpu().numpy(), O.prefill_f64(q, k, v), what=f"prefill 4B-aligned out ({kernel})")
+    assert torch.isnan(buf[:2]).all() and torch.isnan(buf[2 + T * H * D:]).all()
