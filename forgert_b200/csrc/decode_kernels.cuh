@@ -176,9 +176,13 @@ struct SplitSmem {
     static constexpr size_t kRecvFloats = size_t(2 * NT * 8 * 16 + NT * 8 * D + 64);
     // +1024: the ring is realigned to 1024 bytes (128-byte swizzle atom).
     static constexpr size_t kBytes = 1024 + kRecvOffset + kRecvFloats * sizeof(float);
-    // Cross-warp merge area (reuses the ring once every tile is consumed).
-    static constexpr size_t kMergeBytes =
-        size_t(NW) * (NT * 8) * D * sizeof(float) + size_t(NW) * (NT * 8) * 3 * sizeof(float);
+    // Cross-warp merge area (reuses the ring once every tile is consumed):
+    // [NW][GP][kMergeStride] partial accumulators, rows padded by 4 floats so
+    // the 4 lanes of a fragment column (heads 2t, 2t+2, ...) hit different
+    // banks, then [NW][GP][2] (m, l) and [GP][NW] warp weights.
+    static constexpr int kMergeStride = D + 4;
+    static constexpr size_t kMergeBytes = size_t(NW) * (NT * 8) * kMergeStride * sizeof(float) +
+                                          size_t(NW) * (NT * 8) * 3 * sizeof(float);
     // CTA state (acc [GP][D], m [GP], l [GP], flag) read by the cluster through DSMEM.
     static constexpr size_t kStateOffset = (kMergeBytes + 127) / 128 * 128;
     static constexpr size_t kStateBytes = size_t(NT * 8) * (D + 2) * sizeof(float) + 16;
@@ -581,8 +585,9 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         const int ok_all = consumer_sync_and(ok ? 1 : 0, NW * 32);
 
         // ---- cross-warp merge through shared memory -> CTA state
-        float* macc = reinterpret_cast<float*>(smem);                 // [NW][GP][D]
-        float* mml = macc + NW * GP * D;                              // [NW][GP][2]
+        constexpr int MS = S::kMergeStride;
+        float* macc = reinterpret_cast<float*>(smem);                 // [NW][GP][MS]
+        float* mml = macc + NW * GP * MS;                             // [NW][GP][2]
         float* wsc = mml + NW * GP * 2;                               // [GP][NW] warp weights
         if (ok_all) {
 #pragma unroll
@@ -593,7 +598,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                     for (int c = 0; c < 4; ++c) {
                         const int d = dm * 16 + g + ((c >> 1) << 3);
                         const int hj = nt * 8 + 2 * t + (c & 1);
-                        macc[(warp * GP + hj) * D + d] = o[dm][nt][c];
+                        macc[(warp * GP + hj) * MS + d] = o[dm][nt][c];
                     }
             if (g == 0) {
 #pragma unroll
@@ -639,7 +644,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
             const int d = idx % D;
             float acc = 0.f;
 #pragma unroll
-            for (int w = 0; w < NW; ++w) acc = fmaf(macc[(w * GP + hj) * D + d], wsc[hj * NW + w], acc);
+            for (int w = 0; w < NW; ++w) acc = fmaf(macc[(w * GP + hj) * MS + d], wsc[hj * NW + w], acc);
             const size_t hrow = head_base + hj;
             if (p.counters) {
                 st_acc[hj * D + d] = acc;                    // fused: keep the CTA state
