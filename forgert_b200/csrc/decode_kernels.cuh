@@ -612,26 +612,27 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
             }
         }
         consumer_sync(NW * 32);
-        // One thread per head: the max over warps, each warp's weight, l.
-        if (threadIdx.x < GP) {
-            const int hj = threadIdx.x;
-            float mstar = -INFINITY, l = 0.f;
-            if (ok_all) {
+        // One thread per (head, warp), NW adjacent lanes per head: the max
+        // over warps and the weighted l by shuffles, each warp's weight.
+        static_assert((GP * NW) % 32 == 0 && 32 % NW == 0, "whole warps, heads within a warp");
+        if (threadIdx.x < GP * NW) {
+            const int hj = threadIdx.x / NW;
+            const int w = threadIdx.x % NW;
+            const float mw = ok_all ? mml[(w * GP + hj) * 2] : -INFINITY;
+            const float lw = ok_all ? mml[(w * GP + hj) * 2 + 1] : 0.f;
+            float mstar = mw;
 #pragma unroll
-                for (int w = 0; w < NW; ++w) mstar = fmaxf(mstar, mml[(w * GP + hj) * 2]);
-                const float muse = (mstar == -INFINITY) ? 0.f : mstar;
+            for (int o = 1; o < NW; o <<= 1) mstar = fmaxf(mstar, __shfl_xor_sync(0xffffffffu, mstar, o));
+            const float muse = (mstar == -INFINITY) ? 0.f : mstar;
+            const float sc = ok_all ? fast_exp2(mw - muse) : 0.f;
+            wsc[hj * NW + w] = sc;
+            float l = lw * sc;
 #pragma unroll
-                for (int w = 0; w < NW; ++w) {
-                    const float sc = fast_exp2(mml[(w * GP + hj) * 2] - muse);
-                    wsc[hj * NW + w] = sc;
-                    l = fmaf(mml[(w * GP + hj) * 2 + 1], sc, l);
-                }
-            } else {
-#pragma unroll
-                for (int w = 0; w < NW; ++w) wsc[hj * NW + w] = 0.f;
+            for (int o = 1; o < NW; o <<= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            if (w == 0) {
+                st_m[hj] = mstar;
+                st_l[hj] = l;
             }
-            st_m[hj] = mstar;
-            st_l[hj] = l;
         }
         consumer_sync(NW * 32);
 
