@@ -1134,16 +1134,13 @@ int fr_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
     const void* s = device_view(src);
     void* d = const_cast<void*>(device_view(dst));
     if (!s || !d) return FR_ERR_INVALID_ARG;
+    DeviceState* st = nullptr;
+    int rc = get_state(&st);
+    if (rc != FR_OK) return rc;
     const bool vec = aligned(s, 16) && aligned(d, 16);
     const size_t units = vec ? bytes / 16 : bytes;
     const size_t per_cta = (size_t)fr::kCopyThreads * fr::kCopyUnroll;
-    int sms = 148;
-    {
-        int dev = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess)
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    }
-    const size_t ctas = std::max<size_t>(1, std::min<size_t>(2 * (size_t)sms,
+    const size_t ctas = std::max<size_t>(1, std::min<size_t>(2 * (size_t)st->sm_count,
                                                              (units + per_cta - 1) / per_cta));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctas, 1, 1);
