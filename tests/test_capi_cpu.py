@@ -90,6 +90,15 @@ def test_validation_before_any_cuda_call(lib):
     assert lib.fr_rope_tables(None, None, 16, 64, 1e6, 1.0) == _lib.FR_ERR_INVALID_ARG
     assert lib.fr_rope_append(fake, fake, fake, fake, fake, fake, fake, 1, 8, 2, 64, -1, None) == \
         _lib.FR_ERR_INVALID_ARG
+    # prefill: q/k/v are TMA-copied (16-byte aligned), head_dim in {64, 128}
+    assert lib.fr_prefill_attn(fake + 4, fake, fake, fake, 16, 8, 2, 64, None) == _lib.FR_ERR_MISALIGNED
+    assert lib.fr_prefill_attn(fake, fake, fake, fake, 16, 8, 2, 96, None) == _lib.FR_ERR_UNSUPPORTED
+    assert lib.fr_prefill_workspace_size(0, 8, 64) == 0
+    assert lib.fr_prefill_workspace_size(16, 8, 96) == 0
+    # kernel copy: zero bytes is a no-op, null pointers are refused
+    assert lib.fr_copy_async(fake, fake, 0, None) == _lib.FR_OK
+    assert lib.fr_copy_async(nullp, fake, 16, None) == _lib.FR_ERR_INVALID_ARG
+    assert lib.fr_copy_async(fake, nullp, 16, None) == _lib.FR_ERR_INVALID_ARG
 
 
 def test_python_mirror_raises_like_cuda_check():
