@@ -108,6 +108,10 @@ def test_python_mirror_raises_like_cuda_check():
     assert isinstance(e.value, RuntimeError)
     # the reference's older versions are the same entry point
     assert A.decode_attn_v3_vec is A.decode_attn_v4_flash
+    # copy_async reaches host memory only through a page-locked mapping
+    import torch
+    with pytest.raises(ValueError):
+        A.copy_async(torch.zeros(4), torch.zeros(4))
 
 
 def test_c_header_is_plain_c(tmp_path):
