@@ -49,9 +49,11 @@ SIGNATURES = {
     "fr_exchange_reset": (_i, [_vp, ctypes.c_size_t, _vp]),
     "fr_decode_attn_exchange": (_i, [_vp, _vp, _vp, _i, _vp, _i, _i, _i,
                                      ctypes.POINTER(ctypes.c_void_p), _i, _i, _vp]),
+    "fr_exchange_wait_limit_ms": (_i, []),
     "fr_decode_workspace_size": (ctypes.c_size_t, [_i, _i, _i, _i, _i]),
     "fr_prefill_workspace_size": (ctypes.c_size_t, [_i, _i, _i]),
     "fr_get_device_error": (_i, [_i, ctypes.POINTER(_i)]),
+    "fr_allocated_bytes": (ctypes.c_size_t, []),
     "fr_last_cuda_error": (_i, []),
     "fr_status_string": (ctypes.c_char_p, [_i]),
     "fr_version": (_i, []),

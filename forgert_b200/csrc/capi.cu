@@ -185,9 +185,15 @@ int set_smem_attr() {
     return FR_OK;
 }
 
+// Guards the per-device attribute bits, occupancy and co-residency caches:
+// two host threads making their first call on one device must not race on
+// them.
+std::mutex g_prep_mu;
+
 template <int D, int NT>
 int prepare_kernel(DeviceState* st) {
     constexpr int slot = kernel_slot<D, NT>();
+    std::lock_guard<std::mutex> lk(g_prep_mu);
     if (!(st->attr_done & (1u << slot))) {
         int rc = set_smem_attr<D, NT, 1>();
         if (rc == FR_OK) rc = set_smem_attr<D, NT, 2>();
@@ -390,6 +396,7 @@ int query_resident_clusters(int D, int nt, int cl, DeviceState* st);
 int resident_clusters(int D, int nt, int cl, DeviceState* st) {
     const int slot = (D == 64 ? 0 : 2) + (nt - 1);
     const int li = cl >= 16 ? 4 : cl >= 8 ? 3 : cl >= 4 ? 2 : cl >= 2 ? 1 : 0;
+    std::lock_guard<std::mutex> lk(g_prep_mu);
     int& cached = st->resident[slot][li];
     if (cached < 0) cached = query_resident_clusters(D, nt, cl, st);
     return cached;
@@ -552,12 +559,14 @@ int launch_prefill(DeviceState* st, const fr::PrefillParams& pp, cudaStream_t s)
     using PS = fr::PrefillSmem<D, kStages>;
     auto fn = fr::prefill_kernel<D, kStages>;
     const uint32_t bit = 1u << (D == 64 ? 8 : 9);
+    std::unique_lock<std::mutex> lk(g_prep_mu);
     if (!(st->attr_done & bit)) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(PS::kBytes));
         if (e != cudaSuccess) return cuda_fail(e);
         st->attr_done |= bit;
     }
+    lk.unlock();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(pp.H, (pp.T + PS::kTile - 1) / PS::kTile, 1);
     cfg.blockDim = dim3(160, 1, 1);
@@ -669,12 +678,14 @@ int launch_prefill_tc(DeviceState* st, fr::PrefillParams pp, cudaStream_t s) {
                   "exactly two CTAs per SM: their TMEM columns fill the SM");
     auto fn = fr::prefill_tc_kernel<D, kStages>;
     const uint32_t bit = 1u << (D == 64 ? 10 : 11);
+    std::unique_lock<std::mutex> lk(g_prep_mu);
     if (!(st->attr_done & bit)) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(PS::kBytes));
         if (e != cudaSuccess) return cuda_fail(e);
         st->attr_done |= bit;
     }
+    lk.unlock();
     const int nq = (pp.T + PS::kRows - 1) / PS::kRows;
     PrefillPlan pl = prefill_plan(pp.T, pp.H, st->sm_count);
     if (pl.chunk_tiles > 0) {
@@ -735,6 +746,8 @@ int encode_pair(DecodeParams* p, const void* k, const void* v, int head_dim, int
 }
 
 }  // namespace
+
+int* noalloc_error_word(int dev);   // defined with the allocation-free entry point
 
 extern "C" {
 
@@ -911,6 +924,14 @@ int fr_exchange_reset(void* buf, size_t bytes, void* stream) {
     return e == cudaSuccess ? FR_OK : cuda_fail(e);
 }
 
+// FORGERT_EXCHANGE_WAIT_MS (read once): how long the exchange waits for the
+// other ranks' words, 1 ms .. 5 s, default 1 s.  A longer spin would hold a
+// shared GPU busy for no purpose once a peer is gone.
+int fr_exchange_wait_limit_ms(void) {
+    static const int v = std::min(5000, std::max(1, env_int("FORGERT_EXCHANGE_WAIT_MS", 1000)));
+    return v;
+}
+
 int fr_decode_attn_exchange(const void* q, const void* k_local, const void* v_local,
                             int local_kv_len, void* out, int num_heads, int num_kv_heads,
                             int head_dim, void* const* bufs, int rank, int world, void* stream) {
@@ -935,8 +956,7 @@ int fr_decode_attn_exchange(const void* q, const void* k_local, const void* v_lo
     p.xrank = rank;
     p.xworld = world;
     p.xrows = num_heads;
-    static const int wait_ms = std::min(60000, std::max(1, env_int("FORGERT_EXCHANGE_WAIT_MS", 1000)));
-    p.xwait_ms = wait_ms;
+    p.xwait_ms = fr_exchange_wait_limit_ms();
     return run_decode(p, head_dim, 1, std::max(1, local_kv_len), static_cast<__half*>(out),
                       nullptr, nullptr, 1, static_cast<cudaStream_t>(stream));
 }
@@ -1061,25 +1081,50 @@ size_t fr_prefill_workspace_size(int seq_len, int num_heads, int head_dim) {
 }
 
 int fr_get_device_error(int clear, int* device_code) {
+    // Reads (and optionally clears) the error words of the current device:
+    // the one of the regular entry points and the allocation-free one.  It
+    // creates no per-device state and allocates nothing, so callers of
+    // fr_decode_attn_noalloc can use it too.
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e);
     DeviceState* st = nullptr;
-    int rc = get_state(&st);
-    if (rc != FR_OK) return rc;
-    cudaError_t e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) return cuda_fail(e);
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_dev.find(dev);
+        if (it != g_dev.end() && it->second.err) st = &it->second;
+    }
+    int* words[2] = {st ? st->err : nullptr, noalloc_error_word(dev)};
     int code = 0;
-    e = cudaMemcpy(&code, st->err, sizeof(int), cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) return cuda_fail(e);
-    if (clear && code) {
-        e = cudaMemset(st->err, 0, sizeof(int));
+    for (int* w : words) {
+        if (!w) continue;
+        int c = 0;
+        e = cudaMemcpy(&c, w, sizeof(int), cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) return cuda_fail(e);
-        // an aborted call may have left fused-merge counters behind
-        if (st->ws) {
-            e = cudaMemset(st->ws, 0, std::min(st->ws_bytes, kCounterBytes));
+        if (!code) code = c;
+        if (clear && c) {
+            e = cudaMemset(w, 0, sizeof(int));
             if (e != cudaSuccess) return cuda_fail(e);
         }
     }
+    if (clear && code && st && st->ws) {
+        // an aborted call may have left fused-merge counters behind
+        e = cudaMemset(st->ws, 0, std::min(st->ws_bytes, kCounterBytes));
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
     if (device_code) *device_code = code;
     return code ? FR_ERR_TIMEOUT : FR_OK;
+}
+
+size_t fr_allocated_bytes(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_dev.find(dev);
+    if (it == g_dev.end() || !it->second.err) return 0;
+    return sizeof(int) + it->second.ws_bytes;
 }
 
 int fr_last_cuda_error(void) { return t_last_cuda; }
@@ -1174,44 +1219,48 @@ unsigned long long fr_launch_count(void) { return g_launches.load(std::memory_or
 // framework's memory pool or allocator hooks, plugins loaded where the host
 // owns every device allocation, or a process that must not grow its device
 // footprint after start-up.  For them the split partial states live in this
-// file-scope device array instead of the grown-on-demand workspace.  Every
-// GPU that loads the library holds these FR_NOALLOC_SCRATCH_BYTES until the
-// process exits.
+// file-scope device array instead of the grown-on-demand workspace, and the
+// in-kernel error word beside it replaces the cudaMalloc'd one.  Every GPU
+// that loads the library holds these FR_NOALLOC_SCRATCH_BYTES (+ 4 bytes)
+// until the process exits.
 //
-// Host code must not use the array's name as a device address (on the host
-// it is only a stand-in symbol): the set-up below asks the runtime for the
-// real address with cudaGetSymbolAddress, once per device, with that device
-// current, and passes that pointer to the kernels.
+// Host code must not use the arrays' names as device addresses (on the host
+// they are only stand-in symbols): the set-up below asks the runtime for the
+// real addresses with cudaGetSymbolAddress, once per device, with that device
+// current, and passes those pointers to the kernels.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) unsigned char fr_noalloc_scratch[FR_NOALLOC_SCRATCH_BYTES];
+static __device__ int fr_noalloc_err;
 
 namespace {
 
 struct NoAllocDevice {
     bool ready = false;
-    DeviceState st;              // sm_count / kernel attributes; err stays null
+    DeviceState st;              // sm_count / kernel attributes; st.err unused
     float* scratch = nullptr;    // device address of fr_noalloc_scratch on this device
+    int* err = nullptr;          // device address of fr_noalloc_err on this device
 };
 
 std::mutex g_noalloc_mu;
 std::unordered_map<int, NoAllocDevice> g_noalloc;
 
-// First call on a device: symbol address, SM count, kernel attributes.  No
-// allocation anywhere (cudaGetSymbolAddress, cudaDeviceGetAttribute and
-// cudaFuncSetAttribute allocate nothing).
-int noalloc_setup(NoAllocDevice** out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_fail(e);
-    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+// First call on a device: symbol addresses, SM count, kernel attributes.  No
+// allocation anywhere (cudaGetSymbolAddress, cudaDeviceGetAttribute,
+// cudaFuncSetAttribute and the occupancy query allocate nothing).  The
+// caller holds g_noalloc_mu.
+int noalloc_setup_locked(int dev, NoAllocDevice** out) {
     NoAllocDevice& nd = g_noalloc[dev];
     if (!nd.ready) {
         void* ptr = nullptr;
-        e = cudaGetSymbolAddress(&ptr, fr_noalloc_scratch);
+        cudaError_t e = cudaGetSymbolAddress(&ptr, fr_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e);
+        void* eptr = nullptr;
+        e = cudaGetSymbolAddress(&eptr, fr_noalloc_err);
         if (e != cudaSuccess) return cuda_fail(e);
         e = cudaDeviceGetAttribute(&nd.st.sm_count, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return cuda_fail(e);
         nd.scratch = static_cast<float*>(ptr);
+        nd.err = static_cast<int*>(eptr);
         nd.ready = true;
     }
     *out = &nd;
@@ -1219,6 +1268,14 @@ int noalloc_setup(NoAllocDevice** out) {
 }
 
 }  // namespace
+
+// The no-alloc error word of device `dev` (nullptr when no allocation-free
+// call ran there); read by fr_get_device_error.
+int* noalloc_error_word(int dev) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    auto it = g_noalloc.find(dev);
+    return (it != g_noalloc.end() && it->second.ready) ? it->second.err : nullptr;
+}
 
 extern "C" int fr_decode_attn_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                       void* out, int num_heads, int num_kv_heads, int head_dim,
@@ -1228,14 +1285,25 @@ extern "C" int fr_decode_attn_noalloc(const void* q, const void* k_cache, const 
     if (rc != FR_OK) return rc;
     if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 4) || !aligned(out, 4))
         return FR_ERR_MISALIGNED;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
     NoAllocDevice* nd = nullptr;
-    rc = noalloc_setup(&nd);
-    if (rc != FR_OK) return rc;
     const int group = num_heads / num_kv_heads;
     Plan pl;
-    rc = plan_for(&nd->st, head_dim, 1, num_kv_heads, group, kv_len, 1, &pl);
-    if (rc != FR_OK) return rc;
-    // Same plan as fr_decode_attn; a plan whose partials do not fit is refused.
+    {
+        // Set-up and planning (which sets kernel attributes and caches the
+        // occupancy on first use) under one lock: two host threads making
+        // their first call on a device do not race on those fields.
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        rc = noalloc_setup_locked(dev, &nd);
+        if (rc != FR_OK) return rc;
+        rc = plan_for(&nd->st, head_dim, 1, num_kv_heads, group, kv_len, 1, &pl);
+        if (rc != FR_OK) return rc;
+    }
+    // fr_decode_attn's base split count (one CTA slot per SM) without its
+    // cluster sizing or fused merge; a plan whose partials do not fit is
+    // refused before anything is launched.
     if (pl.num_splits > 1 &&
         partial_bytes(num_heads, pl.num_splits, head_dim) > (size_t)FR_NOALLOC_SCRATCH_BYTES)
         return FR_ERR_SCRATCH_LIMIT;
@@ -1248,7 +1316,7 @@ extern "C" int fr_decode_attn_noalloc(const void* q, const void* k_cache, const 
     p.num_splits = pl.num_splits;
     p.head_groups = pl.head_groups;
     p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
-    p.err = nullptr;
+    p.err = nd->err;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     __half* o = static_cast<__half*>(out);
     const bool direct = pl.num_splits == 1;
@@ -1256,8 +1324,9 @@ extern "C" int fr_decode_attn_noalloc(const void* q, const void* k_cache, const 
         p.write_final = 1;
         p.out = o;
     } else {
-        // Every CTA overwrites its own partial state, so nothing in the
-        // scratch needs clearing between calls.
+        // Every CTA overwrites its own partial slot (with the neutral state
+        // if its bounded wait ran out), so nothing in the scratch needs
+        // clearing between calls.
         p.write_final = 0;
         p.part_ml = nd->scratch;
         p.part_acc = nd->scratch + (size_t)num_heads * pl.num_splits * 2;

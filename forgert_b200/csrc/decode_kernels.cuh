@@ -643,16 +643,22 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
             const int idx = threadIdx.x + it * NW * 32;
             const int hj = idx / D;
             const int d = idx % D;
+            // A CTA whose bounded wait ran out (ok_all == 0, error word set)
+            // carries the neutral state (m = -inf, l = 0, acc = 0) into every
+            // merge, so no merge folds in the merge area's stale contents or a
+            // partial slot left behind by an earlier call.
             float acc = 0.f;
+            if (ok_all) {
 #pragma unroll
-            for (int w = 0; w < NW; ++w) acc = fmaf(macc[(w * GP + hj) * MS + d], wsc[hj * NW + w], acc);
+                for (int w = 0; w < NW; ++w) acc = fmaf(macc[(w * GP + hj) * MS + d], wsc[hj * NW + w], acc);
+            }
             const size_t hrow = head_base + hj;
             if (p.counters) {
                 st_acc[hj * D + d] = acc;                    // fused: keep the CTA state
-            } else if (hj < gcount && ok_all) {
+            } else if (hj < gcount) {
                 const float l = st_l[hj];
                 if (p.write_final) {
-                    p.out[hrow * D + d] = __float2half_rn(l > 0.f ? acc / l : 0.f);
+                    if (ok_all) p.out[hrow * D + d] = __float2half_rn(l > 0.f ? acc / l : 0.f);
                 } else {
                     const size_t slot = hrow * p.part_slots + split;
                     p.part_acc[slot * D + d] = acc;

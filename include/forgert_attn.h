@@ -48,8 +48,8 @@ extern "C" {
 #define FR_ERR_WORKSPACE 6     /* workspace too small while a stream is capturing */
 #define FR_ERR_SCRATCH_LIMIT 7 /* fr_decode_attn_noalloc: partials exceed its static scratch */
 
-/* Size of the static device scratch used by fr_decode_attn_noalloc (2 MiB). */
-#define FR_NOALLOC_SCRATCH_BYTES (2u << 20)
+/* Size of the static device scratch used by fr_decode_attn_noalloc (1 MiB). */
+#define FR_NOALLOC_SCRATCH_BYTES (1u << 20)
 
 /* Single-token decode attention over kv_len cached positions.
  * Replaces decode_attn_v4_flash (kernels/attention.cuh:65-71; definition
@@ -63,19 +63,25 @@ FR_API int fr_decode_attn(const void* q, const void* k_cache, const void* v_cach
  * memory pool, plugins whose host owns every device allocation, processes
  * that must not grow their device footprint after start-up.  No counterpart
  * in the reference (its launchers need no scratch: one CTA per head, no KV
- * split).  Same arguments, results and split plan as fr_decode_attn; the
- * split partial states go to a static 2 MiB device array
- * (FR_NOALLOC_SCRATCH_BYTES) that every GPU loading the library holds until
- * exit.  A call whose partials need more returns FR_ERR_SCRATCH_LIMIT: the
- * need is num_heads * splits * (head_dim + 2) * 4 bytes, e.g. 0.8 MB for
- * 12 heads at kv_len 16384 and 1.1 MB for 28 heads at kv_len 131072, while
- * 32 heads / 2 kv heads / head_dim 128 at kv_len 16384 (2.1 MB) is refused.
- * The first call on a device does a one-time set-up (looks up the array's
- * device address, sets kernel attributes): make that first call before any
+ * split).  Same arguments and results as fr_decode_attn.  It splits the KV
+ * range with fr_decode_attn's base split count (one CTA per SM, without the
+ * thread-block clusters or the fused merge), so its split boundaries can
+ * differ from fr_decode_attn's; the partials go to a static 1 MiB device
+ * array (FR_NOALLOC_SCRATCH_BYTES) and in-kernel errors to a static error
+ * word, both held by every GPU that loads the library until exit.  A call
+ * whose partials need more returns FR_ERR_SCRATCH_LIMIT before launching
+ * anything: the need is num_heads * splits * (head_dim + 2) * 4 bytes with
+ * splits ~ SMs / num_kv_heads, e.g. on a 148-SM B200 0.40 MB for 12 heads /
+ * 2 kv heads at kv_len 16384 and 0.54 MB for 28 / 4 at kv_len 131072, while
+ * 16 heads over one kv head at kv_len 16384 (128 splits, 1.06 MB) is refused.
+ * The first call on a device does a one-time set-up (looks up the arrays'
+ * device addresses, sets kernel attributes): make that first call before any
  * stream capture.  All calls on a device share the one array, so calls that
  * overlap on the GPU (different streams, no ordering) race; serialise them.
- * In-kernel wait timeouts still end the kernel but are not recorded for
- * fr_get_device_error. */
+ * A bounded in-kernel wait that runs out is recorded in the static error
+ * word (read with fr_get_device_error, which allocates nothing); the CTA
+ * concerned contributes an empty partial, so the output is wrong but no
+ * earlier call's scratch is folded in. */
 FR_API int fr_decode_attn_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                   void* out, int num_heads, int num_kv_heads, int head_dim,
                                   int kv_len, void* stream);
@@ -167,9 +173,11 @@ FR_API int fr_lse_merge_strided(const float* states_ml, const float* states_acc,
  * launched.  Each state word is stored with the call's sequence number in
  * one 8-byte access, so a receiver needs no fence or flag: it waits until the
  * words it reads carry its own call number.  If a peer does not take part,
- * the wait ends after about a second (FORGERT_EXCHANGE_WAIT_MS, 1 to 60000,
- * read once per process) with FR_ERR_TIMEOUT from fr_get_device_error; the exchange state is then inconsistent and every rank
- * must fr_exchange_reset its buffer (stream ordered) before the next call.
+ * the wait ends after about a second (FORGERT_EXCHANGE_WAIT_MS, 1 to 5000,
+ * read once per process; fr_exchange_wait_limit_ms() returns the value in
+ * force) with FR_ERR_TIMEOUT from fr_get_device_error; the exchange state is
+ * then inconsistent and every rank must fr_exchange_reset its buffer (stream
+ * ordered) before the next call.
  *   q, out     [num_heads, head_dim] fp16 (the same q on every rank)
  *   k_local, v_local  this GPU's rows [local_kv_len, num_kv_heads, head_dim] */
 FR_API size_t fr_exchange_bytes(int num_heads, int head_dim, int world);
@@ -182,6 +190,7 @@ FR_API int fr_decode_attn_exchange(const void* q, const void* k_local, const voi
                                    int local_kv_len, void* out, int num_heads, int num_kv_heads,
                                    int head_dim, void* const* bufs, int rank, int world,
                                    void* stream);
+FR_API int fr_exchange_wait_limit_ms(void);
 
 /* RoPE cos/sin tables [max_seq_len, head_dim/2] fp32 into caller-allocated
  * device buffers: theta(pos, f) = pos / (base^(2f/head_dim) * scale), evaluated
@@ -239,10 +248,18 @@ FR_API size_t fr_decode_workspace_size(int batch, int num_heads, int num_kv_head
  * fr_reserve_workspace() before capturing a prefill. */
 FR_API size_t fr_prefill_workspace_size(int seq_len, int num_heads, int head_dim);
 
-/* Reads (and optionally clears) the current device's in-kernel error word:
- * 0 = none, otherwise a bounded wait ran out (FR_ERR_TIMEOUT is returned by
- * the status).  Synchronises the device. */
+/* Reads (and optionally clears) the current device's in-kernel error words
+ * (the regular entry points' and fr_decode_attn_noalloc's): 0 = none,
+ * otherwise a bounded wait ran out (FR_ERR_TIMEOUT is returned by the
+ * status).  Synchronises the device; creates no state and allocates
+ * nothing. */
 FR_API int fr_get_device_error(int clear, int* device_code);
+
+/* Device memory the library has allocated with cudaMalloc on the current
+ * device (its error word and workspace; exchange buffers are the caller's),
+ * 0 when none.  Creates no state and allocates nothing.  Diagnostics; no
+ * reference counterpart. */
+FR_API size_t fr_allocated_bytes(void);
 
 /* Last CUDA error code (cudaError_t as int) seen by this thread's calls. */
 FR_API int fr_last_cuda_error(void);

@@ -21,11 +21,13 @@ import pytest
 
 from forgert_b200 import _lib
 from forgert_b200 import attention as A
+from oracle import paths
 
 ROOT = Path(__file__).resolve().parents[1]
 HEADER = ROOT / "include" / "forgert_attn.h"
-REF = Path(os.environ.get("FORGERT_REFERENCE_TREE", "/root/reference"))
-CUDA_INC = "/usr/local/cuda/include"
+REF = paths.reference_tree() or Path("/nonexistent")
+# the CUDA toolkit's headers, next to the nvcc on PATH
+CUDA_INC = str(Path(shutil.which("nvcc") or "nvcc").resolve().parent.parent / "include")
 
 
 def header_symbols():
@@ -157,3 +159,21 @@ def test_reference_executor_compiles_unchanged_against_shim():
     deps = r.stdout
     assert str(ROOT / "include" / "attention.cuh") in deps
     assert str(REF / "kernels" / "attention.cuh") not in deps
+
+
+@pytest.mark.parametrize("env,want", [(None, 1000), ("60000", 5000), ("0", 1), ("250", 250)])
+def test_exchange_wait_limit_is_capped(env, want):
+    """FORGERT_EXCHANGE_WAIT_MS bounds the in-kernel spin on a peer's words;
+    it is clamped to 1 ms .. 5 s (read once per process, so each value runs
+    in a fresh process)."""
+    import sys
+    code = ("import sys; sys.path.insert(0, sys.argv[1]); from forgert_b200 import _lib; "
+            "print(_lib.load().fr_exchange_wait_limit_ms())")
+    e = dict(os.environ)
+    e.pop("FORGERT_EXCHANGE_WAIT_MS", None)
+    if env is not None:
+        e["FORGERT_EXCHANGE_WAIT_MS"] = env
+    r = subprocess.run([sys.executable, "-c", code, str(ROOT)], capture_output=True, text=True,
+                       env=e, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert int(r.stdout.strip()) == want
