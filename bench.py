@@ -2,34 +2,36 @@
 """Decode-attention benchmark (one JSON line on rank 0).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload cfg2|cfg3|cfg3p|cfg4]
+                  [--workload cfg3|cfg2|cfg3p|cfg4|cfg1] [--layers L]
 
-Default workload (cfg2, the configuration the headline metric is quoted on):
-Qwen2-1.5B-shaped decode attention, batch 1, 12 query heads, 2 KV heads,
-head_dim 128, over all 28 layers of a contiguous fp16 cache
-[28 x 2 x 16384 x 2 x 128] (470 MB, N(0,1) synthetic data), once at each
-kv_len in {512, 2048, 4096, 16384}.  One step = those 4 x 28 = 112
-decode_attn_v4_flash-equivalent calls (fr_decode_attn).  Each kv_len group
-is one CUDA graph of 28 calls; L2 is flushed (256 MiB write) before every
-group and the CUDA events bracket only the group, so every K/V byte comes
-from HBM.  metric = algorithmic bytes (K+V of the valid range + q + out)
-per second.
+Headline (default, the same workload at every N): config 3, Qwen2-7B-shaped
+batched decode attention - 64 sequences with ragged kv_len U{1024..8192}
+(seed 2), H28 Hkv4 D128 - as one decode step of the model: its 28 layers'
+attention calls back to back, each layer with its own KV pool, one batched
+call (fr_decode_attn_batched) per layer, captured in one CUDA graph.  The
+256 (sequence, kv head) units are split across the N GPUs
+longest-processing-time first by token count, with no collective on the
+data path; the total work is fixed ("strong").  value = the whole job's
+algorithmic bytes (K+V of the valid range + q + out, every layer) / the
+slowest rank's device time of the step.  A step's K/V (17 GB on one GPU,
+2.1 GB per GPU at N=8) is far larger than L2, and L2 is also flushed (a
+256 MiB write) before every step, outside the CUDA events.
 
-With N > 1 (torchrun) every rank decodes its own sequence (its own cache,
-seeded by rank): batched decode sharded by sequence, no collective on the
-data path; value = all ranks' bytes / the slowest rank's time ("weak").
+Sub-records in the same line (sub.<name>), each with µs/call and GB/s:
+  cfg3_call   one cold batched call of one layer per L2 flush (every N);
+  cfg4        config 4, one 131072-position sequence (H28 Hkv4 D128) over 28
+              layer caches; at N > 1 the KV range is split across the GPUs and
+              the per-head (m, l, acc) states are exchanged inside the split
+              kernel over NVLink (fr_decode_attn_exchange) (every N);
+  cfg2        config 2, H12 Hkv2 D128, 28 layers x kv_len {512, 2048, 4096,
+              16384}, with its own roofline (N = 1);
+  cfg1        config 1, H14 Hkv2 D64 kv_len 512 over the 24 layers of a
+              Qwen2-0.5B cache (N = 1).
 
---workload cfg3 (batched ragged, 64 sequences x 4 kv heads sharded by
-(sequence, kv head) across ranks, "strong") and cfg4 (one 128K-token
-sequence, KV range split across ranks, NCCL all-gather of the per-rank
-(m, l, acc) states + LSE merge, "strong") measure the multi-GPU paths.
---workload cfg3p is cfg3 in a paged KV cache (16-row pages in shuffled order,
-one block table per sequence, fr_decode_attn_paged), sharded by sequence.
-
---impl reference times the reference's own CPU implementation
+--impl reference times the reference's own CPU implementation of the path
 (cpu_decode_attn, tests/test_kernels.cpp:229-270, compiled from the
-reference sources into oracle/_ref) on the same workload with all host
-threads; rank 0 alone runs it.
+reference's sources into oracle/_ref; else the C port under oracle/) on the
+headline workload's shapes with all host threads; rank 0 alone runs it.
 """
 from __future__ import annotations
 
@@ -55,28 +57,33 @@ UNIT = "GB/s"
 L2_FLUSH_BYTES = 256 << 20
 
 
-def parse_args():
+def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours",
                     help="reference = the reference's CPU implementation")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg3p", "cfg4"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg3", "cfg2", "cfg3p", "cfg4", "cfg1"],
+                    default="cfg3")
+    ap.add_argument("--layers", type=int, default=28,
+                    help="cfg3/cfg4: layers decoded back to back per step")
     ap.add_argument("--page-size", type=int, default=16, help="cfg3p page rows (multiple of 16)")
     ap.add_argument("--page-order", choices=["shuffled", "sequential"], default="shuffled",
                     help="cfg3p: pages handed out in a seeded random order, or in order")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="cfg4 at N > 1: in-kernel peer exchange or NCCL all-gather")
-    ap.add_argument("--layers", type=int, default=1,
-                    help="cfg4: layer caches decoded back to back per step (default 1 call)")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of graphs")
     ap.add_argument("--no-overlap", action="store_true",
                     help="disable launch overlap (pre-wait K/V prefetch under PDL)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true", help="headline only, no sub-records")
+    ap.add_argument("--shard", default=None, metavar="N:R",
+                    help="development aid: time rank R's shard of an N-GPU run on this one GPU "
+                         "(the line then describes that shard only)")
     ap.add_argument("--ncu", action="store_true",
-                    help="profiling run: few steps, no clocks/e2e/cpu legs")
-    return ap.parse_args()
+                    help="profiling run: headline only, no clocks/e2e/cpu legs")
+    return ap.parse_args(argv)
 
 
 def dist_env():
@@ -96,15 +103,26 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def traffic_per_launch():
-    """DRAM bytes per launch of the dominant kernel from a committed ncu summary."""
+def traffic_record(key: str):
+    """DRAM bytes per launch of a kernel from a committed ncu summary."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None
     try:
-        return json.loads(p.read_text())
-    except Exception:
+        return json.loads(p.read_text()).get(key)
+    except ValueError:
         return None
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
 
 
 # ------------------------------------------------------------ clock sampler
@@ -183,16 +201,77 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(mhz)}
 
 
-# --------------------------------------------------------------- our arm
+# --------------------------------------------------------------- workloads
+# Each workload knows its shapes without a GPU (config(), used by both arms)
+# and, once built on a device, runs one group of calls per key of `groups`.
+
+def cfg3_config(world: int, layers: int) -> dict:
+    lens = W.cfg3_lens()
+    return {
+        "workload": f"cfg3: Qwen2-7B-shape batched decode attention, 64 sequences, ragged kv_len "
+                    f"U{{1024..8192}} (seed 2), {layers} layers per step, sharded by "
+                    f"(sequence, kv head)",
+        "shape": "Qwen2-7B attention (H28, Hkv4, D128), random data",
+        "global_batch": 64, "num_heads": 28, "num_kv_heads": 4, "head_dim": 128,
+        "layers": layers, "total_kv_tokens_per_layer": int(lens.sum()),
+        "parallelism": f"{world} GPU(s), (sequence, kv head) units by LPT on token count, "
+                       f"no collective",
+        "l2": "step K/V far larger than L2; L2 also flushed (256 MiB write) before each step, "
+              "outside the events",
+    }
+
+
+def cfg2_config(world: int) -> dict:
+    return {
+        "workload": "cfg2: Qwen2-1.5B-shape decode attention, batch 1 per GPU, 28 layers x "
+                    "kv_len {512, 2048, 4096, 16384}",
+        "shape": "Qwen2-1.5B attention (H12, Hkv2, D128), random data",
+        "global_batch": world, "num_heads": 12, "num_kv_heads": 2, "head_dim": 128,
+        "layers": 28, "kv_lens": list(W.CFG2_KV_LENS),
+        "parallelism": f"{world} GPU(s), one sequence per GPU (weak)",
+        "l2": "flushed (256 MiB write) before each kv_len group, outside the events",
+    }
+
+
+def cfg4_config(world: int, layers: int, exchange: str) -> dict:
+    ex = "single GPU" if world == 1 else {
+        "peer": "in-kernel peer stores over NVLink + merge (fr_decode_attn_exchange)",
+        "nccl": "NCCL all-gather + merge kernel"}[exchange]
+    return {
+        "workload": f"cfg4: Qwen2-7B-shape long-context decode attention, 1 sequence, kv_len "
+                    f"131072, {layers} layer(s) per step, KV range split across GPUs",
+        "shape": "Qwen2-7B attention (H28, Hkv4, D128), random data",
+        "global_batch": 1, "num_heads": 28, "num_kv_heads": 4, "head_dim": 128,
+        "kv_len": 131072, "layers": layers, "exchange": ex,
+        "parallelism": f"{world} GPU(s), contiguous KV ranges, (m, l, acc) states exchanged",
+        "l2": "flushed (256 MiB write) before each step, outside the events; N > 1: ranks "
+              "aligned by a one-element all-reduce after the flush",
+    }
+
+
+def cfg1_config(world: int) -> dict:
+    return {
+        "workload": "cfg1: Qwen2-0.5B-shape decode attention, kv_len 512, the 24 layers of one "
+                    "decode step",
+        "shape": "Qwen2-0.5B attention (H14, Hkv2, D64), random data",
+        "global_batch": 1, "num_heads": 14, "num_kv_heads": 2, "head_dim": 64, "kv_len": 512,
+        "layers": 24, "parallelism": "1 GPU",
+        "l2": "flushed (256 MiB write) before each step, outside the events",
+    }
+
+
 class Cfg2:
     """28 layers x kv_len {512, 2048, 4096, 16384}, one sequence per rank."""
 
     L, S, H, HKV, D = W.CFG2_LAYERS, W.CFG2_MAX_SEQ, 12, 2, 128
+    scaling = "weak"
+    graphable = True
+    align_ranks = False
 
-    def __init__(self, torch, rank: int, device):
-        self.torch = torch
+    def __init__(self, torch, rank: int, world: int, device):
         g = torch.Generator(device=device)
         g.manual_seed(1 + 1000 * rank)
+        self.world = world
         self.cache = torch.empty((self.L, 2, self.S, self.HKV, self.D), dtype=torch.float16,
                                  device=device)
         self.cache.normal_(generator=g)
@@ -203,14 +282,14 @@ class Cfg2:
         self.q_host = self.q.cpu().pin_memory()
         self.out_host = torch.empty_like(self.q_host).pin_memory()
 
-    def bytes_per_group(self, kv: int) -> int:
-        return self.L * W.decode_bytes([kv], self.H, self.HKV, self.D)
-
-    def bytes_per_step(self) -> int:
-        return sum(self.bytes_per_group(kv) for kv in self.groups)
+    def call_bytes(self, kv) -> int:
+        return W.decode_bytes([kv], self.H, self.HKV, self.D)
 
     def calls_per_group(self) -> int:
         return self.L
+
+    def job_bytes_per_step(self) -> int:
+        return sum(self.call_bytes(kv) * self.L for kv in self.groups) * self.world
 
     def workspace_bytes(self, A) -> int:
         return max(A.decode_workspace_size(1, self.H, self.HKV, self.D, kv) for kv in self.groups)
@@ -221,112 +300,109 @@ class Cfg2:
                                    self.H, self.HKV, self.D, kv, stream)
 
     def e2e_bytes(self):
-        per = self.H * self.D * 2
-        n = self.L * len(self.groups)
-        return n * per, n * per
-
-    scaling = "weak"
-    graphable = True
-
-    def call_bytes(self, kv: int) -> int:
-        return W.decode_bytes([kv], self.H, self.HKV, self.D)
+        per = self.L * self.H * self.D * 2 * len(self.groups)
+        return per, per
 
     def config(self):
-        return {
-            "workload": "cfg2: Qwen2-1.5B-shape decode attention, batch 1 per GPU, "
-                        "28 layers x kv_len {512, 2048, 4096, 16384}",
-            "shape": "Qwen2-1.5B attention (H12, Hkv2, D128), random data",
-            "batch_per_gpu": 1, "num_heads": self.H, "num_kv_heads": self.HKV,
-            "head_dim": self.D, "layers": self.L, "kv_lens": self.groups,
-            "cache": "contiguous fp16 [28 x 2 x 16384 x 2 x 128] per GPU",
-            "l2": "flushed (256 MiB write) before each kv_len group; events exclude the flush",
-        }
+        return cfg2_config(self.world)
+
+
+class Cfg1(Cfg2):
+    """Config 1's shape over the 24 layers of a Qwen2-0.5B cache at kv_len 512."""
+
+    L, S, H, HKV, D = 24, 512, 14, 2, 64
+
+    def __init__(self, torch, rank: int, world: int, device):
+        g = torch.Generator(device=device)
+        g.manual_seed(0)
+        self.world = world
+        self.cache = torch.empty((self.L, 2, self.S, self.HKV, self.D), dtype=torch.float16,
+                                 device=device).normal_(generator=g)
+        self.q = torch.empty((self.L, self.H, self.D), dtype=torch.float16,
+                             device=device).normal_(generator=g)
+        self.out = torch.empty_like(self.q)
+        self.groups = [512]
+
+    def config(self):
+        return cfg1_config(self.world)
 
 
 class Cfg3:
     """Qwen2-7B batched decode: 64 sequences, kv_len ~ U{1024..8192} (seed 2),
-    H28 Hkv4 D128.  The 256 (sequence, kv head) units are assigned to ranks
-    by LPT on token count; each rank keeps its units in one KV pool
-    [rows, 1, 128] (a unit is one kv head with its 7 query heads) and runs one
-    batched call.  Total work is fixed ("strong")."""
+    H28 Hkv4 D128, `layers` layers per step.  The 256 (sequence, kv head)
+    units are assigned to ranks by LPT on token count; each rank keeps its
+    units in one KV pool per layer [rows, 1, 128] (a unit is one kv head with
+    its 7 query heads) and makes one batched call per layer."""
 
     H, HKV, D, G = 28, 4, 128, 7
     scaling = "strong"
     graphable = True
+    align_ranks = False
 
-    def __init__(self, torch, rank: int, world: int, device):
+    def __init__(self, torch, rank: int, world: int, device, layers: int = 1):
         from forgert_b200 import sharding as SH
-        self.torch = torch
+        self.world = world
+        self.L = max(1, layers)
         self.lens_all = W.cfg3_lens()
         mine = SH.shard_batched(self.lens_all, self.HKV, world)[rank]
-        self.units = mine
         lens = [u[2] for u in mine]
         self.U = len(mine)
         rows = int(sum(lens))
         offs = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
         g = torch.Generator(device=device)
         g.manual_seed(2 + 1000 * rank)
-        self.kpool = torch.empty((rows, 1, self.D), dtype=torch.float16, device=device).normal_(generator=g)
-        self.vpool = torch.empty((rows, 1, self.D), dtype=torch.float16, device=device).normal_(generator=g)
+        shp = (self.L, rows, 1, self.D)
+        self.kpool = torch.empty(shp, dtype=torch.float16, device=device).normal_(generator=g)
+        self.vpool = torch.empty(shp, dtype=torch.float16, device=device).normal_(generator=g)
         self.offs = torch.from_numpy(offs).to(device)
         self.lens = torch.tensor(lens, dtype=torch.int32, device=device)
-        self.q = torch.empty((self.U, self.G, self.D), dtype=torch.float16, device=device).normal_(generator=g)
+        self.q = torch.empty((self.L, self.U, self.G, self.D), dtype=torch.float16,
+                             device=device).normal_(generator=g)
         self.out = torch.empty_like(self.q)
         self.rows = rows
         self.max_len = int(max(lens))
-        self.groups = ["batch"]
-        self.my_bytes = W.decode_bytes(lens, self.G, 1, self.D)
+        self.groups = ["step"]
+        self.my_call_bytes = W.decode_bytes(lens, self.G, 1, self.D)
         self.q_host = self.q.cpu().pin_memory()
         self.out_host = torch.empty_like(self.q_host).pin_memory()
 
-    def bytes_per_group(self, key) -> int:
-        return self.my_bytes
-
-    def bytes_per_step(self) -> int:
-        return self.my_bytes
-
-    def job_bytes(self) -> int:
-        return W.decode_bytes(self.lens_all, self.H, self.HKV, self.D)
-
-    def call_bytes(self, key) -> int:
-        return self.my_bytes
+    def call_bytes(self, key=None) -> int:
+        return self.my_call_bytes
 
     def calls_per_group(self) -> int:
-        return 1
+        return self.L
+
+    def job_bytes_per_step(self) -> int:
+        return W.decode_bytes(self.lens_all, self.H, self.HKV, self.D) * self.L
 
     def workspace_bytes(self, A) -> int:
         return A.decode_workspace_size(self.U, self.G, 1, self.D, self.max_len)
 
     def run_group(self, A, key, stream) -> None:
-        A.decode_attn_batched(self.q, self.kpool, self.vpool, self.offs, self.lens, self.out,
-                              self.U, self.G, 1, self.D, self.rows, self.max_len, stream)
+        for l in range(self.L):
+            A.decode_attn_batched(self.q[l], self.kpool[l], self.vpool[l], self.offs, self.lens,
+                                  self.out[l], self.U, self.G, 1, self.D, self.rows, self.max_len,
+                                  stream)
 
     def e2e_bytes(self):
-        n = self.U * self.G * self.D * 2
+        n = self.L * self.U * self.G * self.D * 2
         return n, n
 
     def config(self):
-        return {
-            "workload": "cfg3: Qwen2-7B-shape batched decode attention, 64 sequences, ragged "
-                        "kv_len U{1024..8192} (seed 2), sharded by (sequence, kv head)",
-            "shape": "Qwen2-7B attention (H28, Hkv4, D128), random data",
-            "global_batch": 64, "num_heads": self.H, "num_kv_heads": self.HKV,
-            "head_dim": self.D, "total_kv_tokens": int(self.lens_all.sum()),
-            "units_this_rank": self.U,
-            "l2": "flushed (256 MiB write) before each call; events exclude the flush",
-        }
+        return cfg3_config(self.world, self.L)
 
 
 class Cfg3Paged(Cfg3):
     """cfg3's 64 sequences in a paged KV cache: pages of page_size rows x 4 kv heads
     x 128, handed out in a seeded random order (a fragmented serving cache),
-    one block table per sequence, one fr_decode_attn_paged call.  N GPUs:
-    whole sequences are assigned by LPT on length; no collective."""
+    one block table per sequence, one fr_decode_attn_paged call (one layer).
+    N GPUs: whole sequences are assigned by LPT on length; no collective."""
 
     def __init__(self, torch, rank: int, world: int, device, page_size: int = 16,
                  page_order: str = "shuffled"):
         from forgert_b200 import sharding as SH
-        self.torch = torch
+        self.world = world
+        self.L = 1
         self.PAGE = page_size
         self.lens_all = W.cfg3_lens()
         mine = SH.lpt_assign(self.lens_all, world)[rank]
@@ -351,11 +427,12 @@ class Cfg3Paged(Cfg3):
         self.table = torch.from_numpy(table).to(device)
         self.width = width
         self.lens = torch.tensor(lens, dtype=torch.int32, device=device)
-        self.q = torch.empty((self.B, self.H, self.D), dtype=torch.float16, device=device).normal_(generator=g)
+        self.q = torch.empty((self.B, self.H, self.D), dtype=torch.float16,
+                             device=device).normal_(generator=g)
         self.out = torch.empty_like(self.q)
         self.max_len = int(max(lens))
-        self.groups = ["batch"]
-        self.my_bytes = W.decode_bytes(lens, self.H, self.HKV, self.D)
+        self.groups = ["step"]
+        self.my_call_bytes = W.decode_bytes(lens, self.H, self.HKV, self.D)
         self.q_host = self.q.cpu().pin_memory()
         self.out_host = torch.empty_like(self.q_host).pin_memory()
         self.U = self.B
@@ -373,40 +450,37 @@ class Cfg3Paged(Cfg3):
         return n, n
 
     def config(self):
-        c = super().config()
-        c["workload"] = (f"cfg3p: cfg3's 64 sequences in a paged KV cache ({self.PAGE}-row pages in "
-                         f"{self.page_order} order, block table per sequence), sharded by sequence")
-        c.pop("units_this_rank", None)
-        c.update({"page_size": self.PAGE, "page_order": self.page_order,
-                  "sequences_this_rank": self.B,
-                  "num_pages_this_rank": self.num_pages})
+        c = cfg3_config(self.world, 1)
+        c["workload"] = (f"cfg3p: cfg3's 64 sequences in a paged KV cache ({self.PAGE}-row pages "
+                         f"in {self.page_order} order, block table per sequence), one layer, "
+                         f"sharded by sequence")
+        c["page_size"] = self.PAGE
         return c
 
 
 class Cfg4:
-    """Qwen2-7B long context: one sequence, kv_len 131072, H28 Hkv4 D128.
-    One GPU: a plain fr_decode_attn call.  N GPUs: each rank holds a
-    contiguous KV range.  exchange "peer" (default): one
-    fr_decode_attn_exchange kernel per rank computes its states, stores them
-    into every rank's exchange buffer over NVLink and merges what arrives;
-    exchange "nccl": partial kernel, NCCL all-gather of the states, merge
-    kernel.  `layers` > 1 runs that many layer caches back to back in one
-    CUDA graph (a decode step's attention calls) instead of a single call.
-    Total work is fixed ("strong")."""
+    """Qwen2-7B long context: one sequence, kv_len 131072, H28 Hkv4 D128,
+    `layers` layer caches per step.  One GPU: plain fr_decode_attn calls.
+    N GPUs: each rank holds a contiguous KV range; exchange "peer": one
+    fr_decode_attn_exchange kernel per rank and layer computes its states,
+    stores them into every rank's exchange buffer over NVLink and merges what
+    arrives; "nccl": partial kernel, NCCL all-gather of the states, merge
+    kernel.  Total work is fixed ("strong")."""
 
     H, HKV, D, T = 28, 4, 128, 131072
     scaling = "strong"
+    graphable = True
 
     def __init__(self, torch, rank: int, world: int, device, exchange: str = "peer",
-                 layers: int = 1):
+                 layers: int = 1, shard: tuple[int, int] | None = None):
         from forgert_b200 import sharding as SH
-        self.torch = torch
         self.world = world
         self.L = max(1, layers)
-        b, e = SH.kv_ranges(self.T, world)[rank]
+        n_split, r_split = shard if shard else (world, rank)
+        b, e = SH.kv_ranges(self.T, n_split)[r_split]
         self.n = e - b
         g = torch.Generator(device=device)
-        g.manual_seed(3 + 1000 * rank)
+        g.manual_seed(3 + 1000 * r_split)
         self.k = torch.empty((self.L, max(self.n, 1), self.HKV, self.D), dtype=torch.float16,
                              device=device).normal_(generator=g)
         self.v = torch.empty_like(self.k).normal_(generator=g)
@@ -425,25 +499,19 @@ class Cfg4:
             # partial and merge kernels (graphs are released before the
             # process group is destroyed)
             self.dec = SH.LongContextDecoder(self.H, self.HKV, self.D, device)
-        self.graphable = True
-        self.my_bytes = W.decode_bytes([self.n], self.H, self.HKV, self.D)
+        self.my_call_bytes = W.decode_bytes([self.n], self.H, self.HKV, self.D)
         self.q_host = self.q.cpu().pin_memory()
         self.out_host = torch.empty_like(self.q_host).pin_memory()
+        self.n_split = n_split
 
-    def bytes_per_group(self, key) -> int:
-        return self.my_bytes * self.L
-
-    def bytes_per_step(self) -> int:
-        return self.my_bytes * self.L
-
-    def job_bytes(self) -> int:
-        return W.decode_bytes([self.T], self.H, self.HKV, self.D) * self.L
-
-    def call_bytes(self, key) -> int:
-        return self.my_bytes
+    def call_bytes(self, key=None) -> int:
+        return self.my_call_bytes
 
     def calls_per_group(self) -> int:
         return self.L
+
+    def job_bytes_per_step(self) -> int:
+        return W.decode_bytes([self.T], self.H, self.HKV, self.D) * self.L
 
     def workspace_bytes(self, A) -> int:
         return A.decode_workspace_size(1, self.H, self.HKV, self.D, max(self.n, 1))
@@ -461,336 +529,479 @@ class Cfg4:
         return n, n
 
     def config(self):
-        return {
-            "workload": "cfg4: Qwen2-7B-shape long-context decode attention, 1 sequence, "
-                        "kv_len 131072, KV range split across GPUs, (m, l, acc) states "
-                        "exchanged and merged",
-            "exchange": {"none": "single GPU", "peer": "in-kernel peer stores over NVLink + "
-                         "merge (fr_decode_attn_exchange)", "nccl": "NCCL all-gather + merge "
-                         "kernel"}[self.exchange],
-            "shape": "Qwen2-7B attention (H28, Hkv4, D128), random data",
-            "global_batch": 1, "num_heads": self.H, "num_kv_heads": self.HKV,
-            "head_dim": self.D, "kv_len": self.T, "kv_rows_this_rank": self.n,
-            "layers": self.L,
-            "l2": "flushed (256 MiB write) before each step; events exclude the flush",
-            "rank_alignment": "N > 1: one-element NCCL all-reduce after the flush, before "
-                              "the events (ranks start each call together)",
-        }
+        return cfg4_config(self.world, self.L, self.exchange if self.world > 1 else "peer")
+
+    def close(self):
+        if self.dec is not None and hasattr(self.dec, "close"):
+            self.dec.close()       # collective: every rank frees its exchange buffer
+
+
+# ------------------------------------------------------------- timing core
+class Timer:
+    """Warm-up, CUDA-graph capture and event timing of one workload."""
+
+    def __init__(self, ctx, wl, use_graph: bool):
+        self.ctx, self.wl = ctx, wl
+        torch, A, lib, stream = ctx.torch, ctx.A, ctx.lib, ctx.stream
+        A.reserve_workspace(wl.workspace_bytes(A))
+        torch.cuda.synchronize()
+        # eager warm-up (creates the library's device state outside capture)
+        with torch.cuda.stream(stream):
+            for key in wl.groups:
+                wl.run_group(A, key, stream)
+        torch.cuda.synchronize()
+        self.use_graph = use_graph and wl.graphable
+        self.graphs = {}
+        self.launches_per_step = 0
+        if self.use_graph:
+            for key in wl.groups:
+                g = torch.cuda.CUDAGraph()
+                c0 = lib.fr_launch_count()
+                with torch.cuda.graph(g, stream=stream):
+                    wl.run_group(A, key, torch.cuda.current_stream())
+                self.launches_per_step += lib.fr_launch_count() - c0
+                self.graphs[key] = g
+        else:
+            c0 = lib.fr_launch_count()
+            with torch.cuda.stream(stream):
+                for key in wl.groups:
+                    wl.run_group(A, key, stream)
+            torch.cuda.synchronize()
+            self.launches_per_step = lib.fr_launch_count() - c0
+        self.align = (torch.zeros(1, dtype=torch.float32, device=ctx.device)
+                      if ctx.world > 1 and getattr(wl, "align_ranks", False) else None)
+
+    def _group(self, key, body=None):
+        if body is not None:
+            body(key)
+        elif self.use_graph:
+            self.graphs[key].replay()
+        else:
+            self.wl.run_group(self.ctx.A, key, self.ctx.stream)
+
+    def run(self, steps: int, warmup: int, body=None, sampler=None):
+        """Times `steps` steps after `warmup` untimed ones; every group of a
+        step is bracketed by its own events after an L2 flush (and, for
+        workloads whose ranks wait for each other, a rank alignment).
+        Returns (per-group total ms, per-group per-step ms arrays, max-over-
+        ranks total ms)."""
+        ctx, wl = self.ctx, self.wl
+        torch, dist, stream = ctx.torch, ctx.dist, ctx.stream
+
+        def step(events):
+            for i, key in enumerate(wl.groups):
+                ctx.flush.fill_(i & 0xFF)
+                if self.align is not None:
+                    dist.all_reduce(self.align)
+                if events is not None:
+                    events[i][0].record(stream)
+                self._group(key, body)
+                if events is not None:
+                    events[i][1].record(stream)
+
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                step(None)
+        torch.cuda.synchronize()
+        if ctx.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in wl.groups]
+              for _ in range(steps)]
+        if sampler:
+            sampler.__enter__()
+        with torch.cuda.stream(stream):
+            for k in range(steps):
+                step(ev[k])
+        torch.cuda.synchronize()
+        if sampler:
+            sampler.__exit__()
+        if ctx.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        per = {key: np.array([ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(steps)])
+               for i, key in enumerate(wl.groups)}
+        tot = {key: float(v.sum()) for key, v in per.items()}
+        total = sum(tot.values())
+        mx = total
+        if ctx.world > 1:
+            t = torch.tensor([total], dtype=torch.float64, device=ctx.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            mx = float(t.item())
+        assert ctx.A.device_error() == 0, "in-kernel wait timed out"
+        return tot, per, mx
+
+    def release(self):
+        self.graphs.clear()
+
+
+class Ctx:
+    def __init__(self, torch, dist, A, lib, device, stream, flush, rank, world):
+        self.torch, self.dist, self.A, self.lib = torch, dist, A, lib
+        self.device, self.stream, self.flush = device, stream, flush
+        self.rank, self.world = rank, world
+
+
+def group_stats(wl, tot, per, steps, peak):
+    out = {}
+    for key in wl.groups:
+        us = tot[key] * 1e3 / (steps * wl.calls_per_group())
+        gbs = wl.call_bytes(key) / (us * 1e-6) / 1e9
+        p10, p50, p90 = np.percentile(per[key] * 1e3 / wl.calls_per_group(), [10, 50, 90])
+        out[str(key)] = {"us_per_call": round(us, 3), "gbs_per_gpu": round(gbs, 1),
+                         "frac_of_measured_hbm": round(gbs / peak, 4),
+                         "us_per_call_p10_p50_p90": [round(float(p10), 3), round(float(p50), 3),
+                                                     round(float(p90), 3)]}
+    return out
+
+
+def run_sub(ctx, name, make, steps, warmup, use_graph, peak):
+    """One sub-record: build, time, summarise, free."""
+    torch = ctx.torch
+    wl = make()
+    tm = Timer(ctx, wl, use_graph)
+    tot, per, mx = tm.run(steps, warmup)
+    rec = {"config": wl.config(), "steps": steps, "warmup": warmup,
+           "ms_per_step": round(mx / steps, 5),
+           "value": round(wl.job_bytes_per_step() * steps / (mx * 1e-3) / 1e9, 2),
+           "unit": UNIT, "scaling": wl.scaling,
+           "per_call": group_stats(wl, tot, per, steps, peak),
+           "gpu_launches_per_step": int(tm.launches_per_step)}
+    tm.release()
+    if hasattr(wl, "close"):
+        wl.close()
+    del wl, tm
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return rec
 
 
 def run_ours(args, torch, dist, rank, local_rank, world):
-    from forgert_b200 import attention as A
     from forgert_b200 import _lib
+    from forgert_b200 import attention as A
 
     lib = _lib.load()
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    if args.workload == "cfg2":
-        wl = Cfg2(torch, rank, device)
-    elif args.workload == "cfg3":
-        wl = Cfg3(torch, rank, world, device)
-    elif args.workload == "cfg3p":
-        wl = Cfg3Paged(torch, rank, world, device, args.page_size, args.page_order)
-    else:
-        wl = Cfg4(torch, rank, world, device, args.exchange, args.layers)
+    shard = None
+    if args.shard:
+        n, r = (int(x) for x in args.shard.split(":"))
+        shard = (n, r)
+    wrank, wworld = shard[1] if shard else rank, shard[0] if shard else world
+
+    def make(workload, layers):
+        if workload == "cfg2":
+            return Cfg2(torch, wrank, wworld, device)
+        if workload == "cfg1":
+            return Cfg1(torch, wrank, wworld, device)
+        if workload == "cfg3":
+            return Cfg3(torch, wrank, wworld, device, layers)
+        if workload == "cfg3p":
+            return Cfg3Paged(torch, wrank, wworld, device, args.page_size, args.page_order)
+        return Cfg4(torch, rank, world, device, args.exchange, layers, shard=shard)
+
     stream = torch.cuda.Stream(device)
     # Decode-step launch overlap: the attention kernel may stream K/V rows
     # older than the newest one while the preceding kernel finishes.
     lib.fr_set_launch_overlap(0 if args.no_overlap else 1)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
-    A.reserve_workspace(wl.workspace_bytes(A))
-    torch.cuda.synchronize()
+    ctx = Ctx(torch, dist, A, lib, device, stream, flush, rank, world)
+    peak, peak_kind = peaks()
+    use_graph = not args.no_graph
 
-    # Eager warm-up (creates the library's device state outside capture).
-    with torch.cuda.stream(stream):
-        for kv in wl.groups:
-            wl.run_group(A, kv, stream)
-    torch.cuda.synchronize()
-
-    use_graph = not args.no_graph and wl.graphable
-    graphs = {}
-    launches_per_step = 0
-    if use_graph:
-        for kv in wl.groups:
-            g = torch.cuda.CUDAGraph()
-            c0 = lib.fr_launch_count()
-            with torch.cuda.graph(g, stream=stream):
-                wl.run_group(A, kv, torch.cuda.current_stream())
-            launches_per_step += lib.fr_launch_count() - c0
-            graphs[kv] = g
-    else:
-        c0 = lib.fr_launch_count()
-        with torch.cuda.stream(stream):
-            for kv in wl.groups:
-                wl.run_group(A, kv, stream)
-        torch.cuda.synchronize()
-        launches_per_step = lib.fr_launch_count() - c0
-
-    # Workloads whose ranks exchange data inside the timed call (cfg4 at N > 1)
-    # start each call together: a one-element all-reduce after the flush,
-    # outside the events, so the per-rank flush and launch skew is not timed
-    # as waiting for the slowest rank.
-    align = torch.zeros(1, dtype=torch.float32, device=device) \
-        if world > 1 and getattr(wl, "align_ranks", False) else None
-
-    def step(events):
-        for i, kv in enumerate(wl.groups):
-            flush.fill_(i & 0xFF)
-            if align is not None:
-                dist.all_reduce(align)
-            if events is not None:
-                events[i][0].record(stream)
-            if use_graph:
-                graphs[kv].replay()
-            else:
-                wl.run_group(A, kv, stream)
-            if events is not None:
-                events[i][1].record(stream)
-
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            step(None)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-
-    K = args.steps
-    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in wl.groups]
-          for _ in range(K)]
+    # ------------------------------------------------------------ headline
+    wl = make(args.workload, args.layers)
+    tm = Timer(ctx, wl, use_graph)
     sampler = ClockSampler(local_rank) if not args.ncu else None
-    if sampler:
-        sampler.__enter__()
-    with torch.cuda.stream(stream):
-        for k in range(K):
-            step(ev[k])
-    torch.cuda.synchronize()
-    if sampler:
-        sampler.__exit__()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    group_ms = {kv: sum(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(K))
-                for i, kv in enumerate(wl.groups)}
-    total_ms = sum(group_ms.values())
-    assert A.device_error() == 0, "in-kernel wait timed out"
-    max_ms = total_ms
-    if world > 1:
-        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        max_ms = float(t.item())
-    job_bytes = wl.job_bytes() if hasattr(wl, "job_bytes") else wl.bytes_per_step() * world
+    tot, per, max_ms = tm.run(args.steps, args.warmup, sampler=sampler)
+    K = args.steps
+    job_bytes = wl.job_bytes_per_step()
+    if shard:
+        job_bytes = wl.call_bytes(wl.groups[0]) * wl.calls_per_group() * len(wl.groups)
     value = job_bytes * K / (max_ms * 1e-3) / 1e9
+    stats = group_stats(wl, tot, per, K, peak)
 
-    # ---- end to end through the C ABI with pinned host buffers (eager calls)
+    # ---- end to end through the C ABI with pinned host buffers
     e2e = None
-    if not args.ncu:
-        Ke = max(3, min(K, 200))
-        ev2 = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in wl.groups]
-               for _ in range(Ke)]
-        def e2e_body(kv, s):
-            # One decode step's worth of a group: the group's q (every layer)
-            # from pinned host memory, its calls, its outputs back to pinned
-            # host.  Both copies go through fr_copy_async (a kernel that
-            # reaches the page-locked buffers through their device mapping).
+    if not args.ncu and hasattr(wl, "q_host"):
+        def e2e_body(key, s=None):
+            # One decode step's worth of a group: its q (every layer) from
+            # pinned host memory, its calls, its outputs back to pinned host;
+            # both copies through fr_copy_async (a kernel that reaches the
+            # page-locked buffers through their device mapping).
+            s = s or stream
             A.copy_async(wl.q, wl.q_host, stream=s)
-            wl.run_group(A, kv, s)
+            wl.run_group(A, key, s)
             A.copy_async(wl.out_host, wl.out, stream=s)
 
         graphs_e2e = {}
-        if use_graph:
-            for kv in wl.groups:
+        if tm.use_graph:
+            for key in wl.groups:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
-                    e2e_body(kv, torch.cuda.current_stream())
-                graphs_e2e[kv] = g
-
-        def e2e_group(kv):
-            if use_graph:
-                graphs_e2e[kv].replay()
-            else:
-                e2e_body(kv, stream)
-
-        with torch.cuda.stream(stream):
-            for kv in wl.groups:
-                e2e_group(kv)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        with torch.cuda.stream(stream):
-            for k in range(Ke):
-                for i, kv in enumerate(wl.groups):
-                    flush.fill_(i & 0xFF)
-                    if align is not None:
-                        dist.all_reduce(align)
-                    ev2[k][i][0].record(stream)
-                    e2e_group(kv)
-                    ev2[k][i][1].record(stream)
-        torch.cuda.synchronize()
-        e_ms = sum(ev2[k][i][0].elapsed_time(ev2[k][i][1]) for k in range(Ke)
-                   for i in range(len(wl.groups)))
-        if world > 1:
-            t = torch.tensor([e_ms], dtype=torch.float64, device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = float(t.item())
+                    e2e_body(key, torch.cuda.current_stream())
+                graphs_e2e[key] = g
+        body = (lambda key: graphs_e2e[key].replay()) if tm.use_graph else e2e_body
+        Ke = max(3, min(K, 200))
+        _, _, e_ms = tm.run(Ke, 2, body=body)
         h2d, d2h = wl.e2e_bytes()
-        e2e = {"value": job_bytes * Ke / (e_ms * 1e-3) / 1e9, "unit": UNIT,
+        e2e = {"value": round(job_bytes * Ke / (e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "how": "per group of calls (one decode step's layers at one kv_len): one H2D of "
-                      "every layer's q from pinned host, the calls through the C ABI, one D2H "
-                      "of every output to pinned host, the copies by fr_copy_async (a kernel "
-                      "reading/writing the page-locked buffers through their device mapping); "
-                      "all three in one CUDA graph per group unless --no-graph; CUDA events "
-                      "around them, L2 flushed before each group"}
+               "how": "per step: one H2D of every layer's q from pinned host memory, the calls "
+                      "through the C ABI, one D2H of every output to pinned host memory; the "
+                      "copies by fr_copy_async (a kernel that reads/writes the page-locked "
+                      "buffers through their device mapping); all in one CUDA graph per step; "
+                      "CUDA events around them, L2 flushed before each step"}
+        graphs_e2e.clear()
+    tm.release()
+    launches = int(tm.launches_per_step * K)
+    if hasattr(wl, "close"):
+        wl.close()
+    dom_key = wl.groups[-1]
+    head_calls = wl.calls_per_group()
+    head_call_bytes = wl.call_bytes(dom_key)
+    cfg = wl.config()
+    del wl, tm
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
 
-    close = getattr(getattr(wl, "dec", None), "close", None)
-    if close is not None:
-        close()                          # collective: every rank frees its exchange buffer
+    # ------------------------------------------------------- sub-records
+    sub = {}
+    if not args.ncu and not args.no_sub and not shard and args.workload == "cfg3":
+        Ks = max(5, min(K, 50))
+        sub["cfg3_call"] = run_sub(ctx, "cfg3_call", lambda: Cfg3(torch, rank, world, device, 1),
+                                   max(20, min(K, 200)), 5, use_graph, peak)
+        sub["cfg4"] = run_sub(ctx, "cfg4",
+                              lambda: Cfg4(torch, rank, world, device, args.exchange, 28),
+                              Ks, 3, use_graph, peak)
+        if world == 1:
+            sub["cfg2"] = run_sub(ctx, "cfg2", lambda: Cfg2(torch, 0, 1, device), Ks * 4, 5,
+                                  use_graph, peak)
+            c2 = sub["cfg2"]["per_call"]["16384"]
+            tr = traffic_record("cfg2_kv16384")
+            sub["cfg2"]["roofline"] = {
+                "bound": "hbm", "kernel": "split_decode_kernel (one fr_decode_attn call, merge "
+                                          "fused), kv_len 16384",
+                "achieved": c2["gbs_per_gpu"], "peak": peak, "unit": "GB/s",
+                "frac": round(c2["gbs_per_gpu"] / peak, 4), "peak_kind": peak_kind,
+                "traffic": tr.get("dram_bytes_per_launch") if tr else None,
+                "algorithmic_bytes_per_launch": W.decode_bytes([16384], 12, 2, 128)}
+            sub["cfg1"] = run_sub(ctx, "cfg1", lambda: Cfg1(torch, 0, 1, device), Ks * 4, 5,
+                                  use_graph, peak)
     if rank != 0:
         return
-    peak, peak_kind = peaks()
-    sweep = {}
-    for kv in wl.groups:
-        us = group_ms[kv] * 1e3 / (K * wl.calls_per_group())
-        gbs = wl.call_bytes(kv) / (us * 1e-6) / 1e9
-        i = wl.groups.index(kv)
-        per_step = np.array([ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(K)]) * 1e3 / \
-            wl.calls_per_group()
-        p10, p50, p90 = np.percentile(per_step, [10, 50, 90])
-        sweep[str(kv)] = {"us_per_call": round(us, 3), "gbs": round(gbs, 1),
-                          "frac_of_measured_hbm": round(gbs / peak, 4),
-                          "us_per_call_p10_p50_p90": [round(float(p10), 3), round(float(p50), 3),
-                                                      round(float(p90), 3)]}
-    dom = str(wl.groups[-1])
-    tr = traffic_per_launch() if args.workload == "cfg2" else None
+
+    tr = traffic_record(f"{args.workload}_call") if args.workload in ("cfg3", "cfg4") else \
+        traffic_record("cfg2_kv16384") if args.workload == "cfg2" else None
+    achieved = head_call_bytes / (stats[str(dom_key)]["us_per_call"] * 1e-6) / 1e9
+    kern = {"cfg3": "split_decode_kernel, batched (fr_decode_attn_batched): one call per layer",
+            "cfg3p": "split_decode_kernel, paged (fr_decode_attn_paged)",
+            "cfg4": "split_decode_kernel (fr_decode_attn / fr_decode_attn_exchange), one call "
+                    "per layer",
+            "cfg2": "split_decode_kernel (fr_decode_attn), kv_len 16384",
+            "cfg1": "split_decode_kernel (fr_decode_attn), kv_len 512"}[args.workload]
     roofline = {
-        "bound": "hbm",
-        "kernel": f"split_decode_kernel (one fr_decode_attn call, merge fused), kv_len {dom}",
-        "achieved": sweep[dom]["gbs"], "peak": peak, "unit": "GB/s",
-        "frac": round(sweep[dom]["gbs"] / peak, 4), "peak_kind": peak_kind,
-        "traffic": tr.get("dram_bytes_per_launch") if tr else None,
-        "algorithmic_bytes_per_launch": wl.call_bytes(wl.groups[-1]),
+        "bound": "hbm", "kernel": kern, "achieved": round(achieved, 1), "peak": peak,
+        "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+        "traffic": (tr.get("dram_bytes_per_launch") if tr else None),
+        "traffic_scope": (tr.get("scope") if tr else None),
+        "algorithmic_bytes_per_launch": head_call_bytes,
+        "how": "achieved = algorithmic bytes of one call on this GPU / (device time of the "
+               "timed steps / calls per step); rank 0's calls",
     }
-    cfg = wl.config()
-    par = {"cfg2": f"dp{world} (one sequence per GPU)",
-           "cfg3": f"{world} GPUs, (sequence, kv head) units by LPT, no collective",
-           "cfg3p": f"{world} GPUs, sequences by LPT, no collective",
-           "cfg4": f"{world} GPUs, KV range split, states exchanged ({args.exchange})"}[args.workload]
-    cfg.update({"parallelism": par, "graph": use_graph,
-                "launch_overlap": not args.no_overlap, "sweep": sweep})
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(max_ms / K, 5), "higher_is_better": True,
-        "scaling": wl.scaling, "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
-        "data": "synthetic N(0,1) fp16", "config": cfg, "roofline": roofline,
-        "gpu_launches": int(launches_per_step * K), "e2e": e2e,
+        "scaling": "strong" if args.workload in ("cfg3", "cfg4", "cfg3p") else "weak",
+        "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+        "data": "synthetic N(0,1) fp16", "config": cfg,
+        "per_call": stats, "calls_per_step": head_calls,
+        "method": {"graph": use_graph, "launch_overlap": not args.no_overlap},
+        "roofline": roofline, "gpu_launches": launches, "e2e": e2e,
         "clocks": sampler.summary() if sampler else None,
     }
-    if world == 1 and not args.no_cpu_baseline and not args.ncu and args.workload == "cfg2":
-        line["cpu_baseline"] = cpu_baseline_cfg2(budget_s=12.0)
+    if shard:
+        line["shard"] = {"of_gpus": shard[0], "rank": shard[1],
+                         "note": "one rank's shard timed alone on one GPU; value = this shard's "
+                                 "bytes / its time, not a whole-job figure"}
+    if sub:
+        line["sub"] = sub
+    if world == 1 and not shard and not args.no_cpu_baseline and not args.ncu and \
+            args.workload == "cfg3":
+        line["cpu_baseline"] = cpu_baseline_cfg3(budget_s=12.0)
+        line["cpu_baseline_hf"] = cpu_baseline_hf_cfg3(budget_s=8.0)
     emit(line)
 
 
 # --------------------------------------------------------- reference arm
-def _cfg2_host_problem(layers):
-    """fp32 copies of cfg2 layers (K, V [16384, 2, 128]) and q per layer."""
-    data = []
-    for l in layers:
-        k, v = W.cfg2_layer_kv(l)
-        q = W.cfg2_layer_q(l)
-        data.append((np.ascontiguousarray(q, np.float32), np.ascontiguousarray(k, np.float32),
-                     np.ascontiguousarray(v, np.float32)))
-    return data
-
-
 class _RefRunner:
-    """cpu_decode_attn calls over all host threads (oracle/_ref), else the C port."""
+    """cpu_decode_attn (the reference's own CPU path, oracle/_ref; else the C
+    port) over a list of calls, one host thread per core pulling calls off a
+    queue longest first, so no thread idles while long calls remain."""
 
-    def __init__(self, data, kv_lens):
+    def __init__(self, calls, H, Hkv, D):
         from oracle import oracle as O
 
-        self.O = O
         self.lib = O.load_ref()
         self.kind = "reference" if self.lib is not None else "port"
+        self.fn = (self.lib.ref_cpu_decode_attn if self.lib is not None
+                   else O.load_oracle().oracle_decode_attn_f32)
         self.threads = os.cpu_count() or 1
-        self.calls = [(q, k, v, kv) for kv in kv_lens for (q, k, v) in data]
-        self.outs = [np.zeros((12, 128), np.float32) for _ in self.calls]
+        self.H, self.Hkv, self.D = H, Hkv, D
+        self.calls = sorted(calls, key=lambda c: -c[3])     # (q, k, v, kv_len)
+        self.outs = [np.zeros((H, D), np.float32) for _ in self.calls]
+
+    def run(self, calls=None):
+        import queue
         f32p = ctypes.POINTER(ctypes.c_float)
-        n = len(self.calls)
-        if self.lib is not None:
-            self.qs = (f32p * n)(*[q.ctypes.data_as(f32p) for q, _, _, _ in self.calls])
-            self.ks = (f32p * n)(*[k.ctypes.data_as(f32p) for _, k, _, _ in self.calls])
-            self.vs = (f32p * n)(*[v.ctypes.data_as(f32p) for _, _, v, _ in self.calls])
-            self.os_ = (f32p * n)(*[o.ctypes.data_as(f32p) for o in self.outs])
-            self.lens = (ctypes.c_int * n)(*[kv for _, _, _, kv in self.calls])
+        idx = range(len(self.calls)) if calls is None else calls
+        qu = queue.SimpleQueue()
+        for i in idx:
+            qu.put(i)
 
-    def run(self):
-        if self.lib is not None:
-            self.lib.ref_cpu_decode_attn_many(self.qs, self.ks, self.vs, self.os_, self.lens,
-                                              len(self.calls), 12, 2, 128, self.threads)
-            return
-        from concurrent.futures import ThreadPoolExecutor
-        lib = self.O.load_oracle()
-        f32p = ctypes.POINTER(ctypes.c_float)
+        def worker():
+            while True:
+                try:
+                    i = qu.get_nowait()
+                except queue.Empty:
+                    return
+                q, k, v, n = self.calls[i]
+                self.fn(q.ctypes.data_as(f32p), k.ctypes.data_as(f32p), v.ctypes.data_as(f32p),
+                        self.outs[i].ctypes.data_as(f32p), self.H, self.Hkv, self.D, n)
 
-        def one(i):
-            q, k, v, kv = self.calls[i]
-            lib.oracle_decode_attn_f32(q.ctypes.data_as(f32p), k.ctypes.data_as(f32p),
-                                       v.ctypes.data_as(f32p), self.outs[i].ctypes.data_as(f32p),
-                                       12, 2, 128, kv)
+        ts = [threading.Thread(target=worker) for _ in range(self.threads)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
 
-        with ThreadPoolExecutor(self.threads) as ex:
-            list(ex.map(one, range(len(self.calls))))
-
-    def bytes(self):
-        return sum(W.decode_bytes([kv], 12, 2, 128) for _, _, _, kv in self.calls)
+    def bytes(self, calls=None):
+        idx = range(len(self.calls)) if calls is None else calls
+        return sum(W.decode_bytes([self.calls[i][3]], self.H, self.Hkv, self.D) for i in idx)
 
 
-def cpu_baseline_cfg2(budget_s: float):
-    """Bounded sample: 4 layers x the 4 kv_lens, repeated for about budget_s."""
-    runner = _RefRunner(_cfg2_host_problem(range(4)), W.CFG2_KV_LENS)
+def _cfg3_host_calls(max_seqs=None):
+    """fp32 host copies of cfg3's sequences (q [28,128], K/V [len,4,128])."""
+    lens, q, ks, vs = W.cfg3_inputs(max_seqs=max_seqs)
+    return [(np.ascontiguousarray(q[b], np.float32), np.ascontiguousarray(ks[b], np.float32),
+             np.ascontiguousarray(vs[b], np.float32), int(lens[b])) for b in range(len(ks))]
+
+
+def _sample_for(runner, budget_s, min_frac=0.25):
+    """Calls of a bounded sample: every call (one layer of the batch) when one
+    pass fits the budget, else the longest-first prefix that does, at least
+    `min_frac` of the calls, interleaved long and short."""
+    t0 = time.perf_counter()
+    runner.run()
+    one = time.perf_counter() - t0
+    n = len(runner.calls)
+    if one <= budget_s:
+        return list(range(n)), one
+    k = max(int(n * min_frac), int(n * budget_s / one))
+    order = [i for pair in zip(range(n), range(n - 1, -1, -1)) for i in pair]
+    seen, out = set(), []
+    for i in order:
+        if i not in seen:
+            seen.add(i)
+            out.append(i)
+        if len(out) >= k:
+            break
+    return out, one
+
+
+def cpu_baseline_cfg3(budget_s: float):
+    """The reference's cpu_decode_attn over one layer of cfg3's 64 sequences,
+    repeated for about budget_s on all host threads."""
+    runner = _RefRunner(_cfg3_host_calls(), 28, 4, 128)
+    runner.run()                                   # warm (page in the inputs)
     t0 = time.perf_counter()
     reps = 0
     while True:
         runner.run()
         reps += 1
         el = time.perf_counter() - t0
-        if el >= budget_s or reps >= 2000:
+        if el >= budget_s or reps >= 1000:
             break
     return {"value": round(runner.bytes() * reps / el / 1e9, 4), "unit": UNIT,
-            "cores": runner.threads, "kind": runner.kind,
-            "sample": f"cfg2 layers 0-3 x kv_len {{512,2048,4096,16384}} (16 calls) x {reps} reps, "
-                      f"{el:.1f} s; cpu_decode_attn (tests/test_kernels.cpp:229-270) on "
-                      f"{runner.threads} threads"}
+            "cores": runner.threads, "cpu": cpu_model(), "kind": runner.kind,
+            "sample": f"one layer of cfg3 (64 sequences, H28 Hkv4 D128, ragged kv_len) x {reps} "
+                      f"reps, {el:.1f} s; cpu_decode_attn (tests/test_kernels.cpp:229-270) per "
+                      f"sequence on {runner.threads} threads, longest sequences first from a "
+                      f"shared queue; fp32 inputs as that function takes them"}
+
+
+def cpu_baseline_hf_cfg3(budget_s: float):
+    """transformers' eager attention (python/reference.py's arithmetic:
+    Qwen2 eager_attention_forward, fp16 on CPU, probabilities rounded to fp16)
+    on cfg3 sequences, torch threads = all host cores."""
+    try:
+        import torch
+        from transformers.models.qwen2.modeling_qwen2 import eager_attention_forward
+    except Exception as e:        # pragma: no cover - transformers is in the image
+        return {"unavailable": f"transformers not importable: {e}"}
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+
+    class _Mod(torch.nn.Module):
+        num_key_value_groups = 7
+
+    mod = _Mod().eval()
+    lens, q, ks, vs = W.cfg3_inputs(max_seqs=16)
+    tq = [torch.from_numpy(q[b]).view(1, 28, 1, 128) for b in range(len(ks))]
+    tk = [torch.from_numpy(np.ascontiguousarray(k.transpose(1, 0, 2)))[None] for k in ks]
+    tv = [torch.from_numpy(np.ascontiguousarray(v.transpose(1, 0, 2)))[None] for v in vs]
+    scaling = 128 ** -0.5
+    with torch.no_grad():
+        eager_attention_forward(mod, tq[0], tk[0], tv[0], None, scaling)
+        t0 = time.perf_counter()
+        done = 0
+        nbytes = 0
+        while True:
+            for b in range(len(ks)):
+                eager_attention_forward(mod, tq[b], tk[b], tv[b], None, scaling)
+                nbytes += W.decode_bytes([int(lens[b])], 28, 4, 128)
+            done += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s or done >= 1000:
+                break
+    return {"value": round(nbytes / el / 1e9, 4), "unit": UNIT, "cores": threads,
+            "cpu": cpu_model(), "kind": "reference",
+            "sample": f"cfg3 sequences 0-15 (H28 Hkv4 D128) x {done} reps, {el:.1f} s; "
+                      f"transformers Qwen2 eager_attention_forward (python/reference.py's "
+                      f"attention), fp16 CPU tensors, torch.set_num_threads({threads})"}
 
 
 def run_reference(args, rank, world):
+    """The reference's CPU path on the headline workload's shapes (cfg3): one
+    step = one layer of the 64-sequence batch (or, when K+W such steps would
+    exceed about a minute, a bounded longest-and-shortest sample of it)."""
     if rank != 0:
         return
-    if args.workload != "cfg2":
-        emit({"impl": "reference", "unavailable": f"reference arm implemented for cfg2 only"})
+    if args.workload != "cfg3":
+        emit({"impl": "reference", "unavailable": "reference arm implemented for the default "
+                                                  "workload (cfg3) only"})
         return
-    runner = _RefRunner(_cfg2_host_problem(range(W.CFG2_LAYERS)), W.CFG2_KV_LENS)
+    runner = _RefRunner(_cfg3_host_calls(), 28, 4, 128)
+    budget = 60.0 / max(1, args.steps + args.warmup)
+    calls, one = _sample_for(runner, budget)
     for _ in range(args.warmup):
-        runner.run()
+        runner.run(calls)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        runner.run()
+        runner.run(calls)
     el = time.perf_counter() - t0
-    value = runner.bytes() * args.steps / el / 1e9
+    value = runner.bytes(calls) * args.steps / el / 1e9
+    sample = (f"{len(calls)} of cfg3's 64 sequences (one layer, H28 Hkv4 D128) per step; "
+              f"cpu_decode_attn (tests/test_kernels.cpp:229-270) per sequence on "
+              f"{runner.threads} threads, longest first from a shared queue")
     emit({
-        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el * 1e3 / args.steps, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "fp32 (fp16-valued inputs)", "data": "synthetic N(0,1) fp16",
-        "impl": "reference",
-        "config": {"workload": "cfg2: Qwen2-1.5B-shape decode attention, batch 1 per GPU, 28 "
-                               "layers x kv_len {512, 2048, 4096, 16384}",
-                   "num_heads": 12, "num_kv_heads": 2, "head_dim": 128, "layers": 28,
-                   "kv_lens": list(W.CFG2_KV_LENS)},
+        "impl": "reference", "config": cfg3_config(world, args.layers),
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": runner.threads,
-                         "kind": runner.kind,
-                         "sample": "full cfg2 step (112 cpu_decode_attn calls) per step"},
+                         "cpu": cpu_model(), "kind": runner.kind, "sample": sample},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     })

@@ -39,11 +39,20 @@ def needs_build() -> bool:
     return any(p.stat().st_mtime > t for p in SOURCES + HEADERS)
 
 
-def build(verbose: bool = False, force: bool = False) -> Path:
-    if not force and not needs_build():
+# The trace variant (per-CTA phase timestamps, forgert_b200/phase_trace.py):
+# the same sources with -DFR_TRACE, never loaded unless FORGERT_B200_LIB
+# names it.
+TRACE_LIB_PATH = PKG_DIR / "libforgert_b200_trace.so"
+
+
+def build(verbose: bool = False, force: bool = False, trace: bool = False) -> Path:
+    out = TRACE_LIB_PATH if trace else LIB_PATH
+    if not force and not trace and not needs_build():
         return LIB_PATH
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = out.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS]
+    if trace:
+        cmd += ["-DFR_TRACE"]
     if verbose:
         cmd += ["-Xptxas", "-v"]
     cmd += [str(s) for s in SOURCES] + ["-o", str(tmp), "-lcudart"]
@@ -52,10 +61,9 @@ def build(verbose: bool = False, force: bool = False) -> Path:
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{' '.join(cmd)}\n{res.stderr}")
     if verbose:
         sys.stderr.write(res.stderr)
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":
-    build(verbose="--verbose" in sys.argv, force=True)
-    print(LIB_PATH)
+    print(build(verbose="--verbose" in sys.argv, force=True, trace="--trace" in sys.argv))

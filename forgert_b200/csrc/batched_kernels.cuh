@@ -1,0 +1,575 @@
+// batched_kernels.cuh - persistent, load-balanced decode over a ragged batch.
+//
+// Serves fr_decode_attn_batched: B sequences of different lengths in one KV
+// pool, every (sequence, kv head, head group) "unit" needing its own
+// softmax.  (The reference decodes one sequence per call,
+// kernels/attention_decode.cu:535-556; batching is this library's addition.)
+//
+// Work decomposition (stream-K over K/V tiles).  Every unit is cut into
+// 64-row tiles (at least one, so a zero-length sequence still yields zeros).
+// Concatenating all units' tiles in (sequence, kv head, head group) order
+// gives T tiles; the grid is persistent - C CTAs, as many as are co-resident
+// - and CTA c takes the contiguous tile range [c*T/C, (c+1)*T/C).  Every CTA
+// therefore streams the same number of K/V bytes (within one tile) whatever
+// the length distribution, and no CTA is launched without work.  A CTA's
+// range is a sequence of "items" (the tiles of one unit inside the range):
+// items in the middle of the range cover a whole unit; only the first and the
+// last item can be a piece of a unit that other CTAs share.
+//
+// Per item: the consumer warps keep the split kernel's per-warp online
+// softmax (consume_tile, decode_kernels.cuh), fold their four states through
+// a small shared-memory exchange area in two rounds (warps 2,3 -> 0,1 ->
+// 0), and warp 0 either writes the normalised fp16 output (whole unit) or
+// stores the piece's (m, l, acc) state in the CTA's partial slot (2c for its
+// first item, 2c + 1 for its last) and counts it on the unit's counter; the
+// CTA whose count completes the unit merges every piece (log-sum-exp) into
+// the output and re-arms the counter.  Meanwhile the producer warp keeps
+// streaming the next item's tiles through the TMA ring: the ring never
+// drains at item boundaries.
+//
+// Metadata: every CTA reads kv_lens (B <= kPersistMaxBatch) and forms the
+// tile prefix in shared memory with a block-wide scan; row_offsets are read
+// by the producer one sequence ahead.
+//
+// Launch overlap: the kernel lets the next grid launch at once.  With
+// prefetch_meta set (fr_set_launch_overlap(1) on a non-default stream) it
+// reads kv_lens / row_offsets and streams every tile but each unit's last
+// before its grid-dependency wait; q, the tiles holding a sequence's newest
+// row, and every store wait for the preceding grid.
+#pragma once
+#include "decode_kernels.cuh"
+
+namespace fr {
+
+constexpr int kPersistMaxBatch = 512;   // sequences whose lengths fit the shared-memory prefix
+
+template <int D, int NT, int TILE, int STAGES, int NW>
+struct PersistSmem {
+    static constexpr int kSub = D / 64;
+    static constexpr int kSubBytes = TILE * 128;
+    static constexpr int kTileBytes = kSub * kSubBytes;
+    static constexpr size_t kRingBytes = size_t(2) * STAGES * kTileBytes;
+    // Exchange area of the cross-warp fold: 2 slots x 32 lanes x (the O^T
+    // fragments of one 8-head tile + m, l of its two head columns).
+    static constexpr int kXFloats = (D / 16) * 4 + 4;
+    static constexpr size_t kXOffset = kRingBytes;
+    static constexpr size_t kXBytes = size_t(2) * 32 * kXFloats * sizeof(float);
+    static constexpr size_t kBarOffset = kXOffset + kXBytes;            // full, empty
+    static constexpr size_t kFlagOffset = kBarOffset + 2 * STAGES * sizeof(uint64_t);
+    static constexpr size_t kMetaOffset = kFlagOffset + 16 * sizeof(int);
+    // seq_start [kPersistMaxBatch + 1] (tile prefix x units per sequence),
+    // lens [kPersistMaxBatch], warp sums [8]
+    static constexpr size_t kMetaBytes = (2 * kPersistMaxBatch + 1 + 8) * sizeof(int);
+    // +1024: the ring is realigned to 1024 bytes (128-byte swizzle atom).
+    static constexpr size_t kBytes = 1024 + kMetaOffset + kMetaBytes;
+    static_assert(kSubBytes % 1024 == 0, "swizzled boxes must stay 1024-byte aligned");
+    static_assert(kXFloats % 4 == 0, "exchange rows are float4-stored");
+};
+
+// Tiles per sequence (at least one) as an exclusive prefix in unit tiles
+// (x upb units per sequence): seq_start[0..B]; lens[b] = kv_lens[b].  Every
+// thread of the block takes part.
+template <int TILE>
+__device__ __forceinline__ void scan_lengths(const int* kv_lens, int B, int upb, int* seq_start,
+                                             int* lens, int* warp_sums) {
+    constexpr int kChunks = 4;                      // 4 x 160 threads >= kPersistMaxBatch
+    const int nthr = blockDim.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nwarps = nthr >> 5;
+    int vals[kChunks];
+#pragma unroll
+    for (int r = 0; r < kChunks; ++r) {             // every load in flight at once
+        const int b = r * nthr + tid;
+        vals[r] = b < B ? kv_lens[b] : 0;
+    }
+    int carry = 0;
+#pragma unroll
+    for (int r = 0; r < kChunks; ++r) {
+        if (r * nthr >= B) break;                   // uniform
+        const int b = r * nthr + tid;
+        const int len = max(0, vals[r]);
+        const int n = b < B ? max(1, (len + TILE - 1) / TILE) : 0;
+        int x = n;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) warp_sums[warp] = x;
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int w = 0; w < nwarps; ++w) {
+            const int ws = warp_sums[w];
+            before += w < warp ? ws : 0;
+            total += ws;
+        }
+        if (b < B) {
+            seq_start[b] = (carry + before + x - n) * upb;
+            lens[b] = len;
+        }
+        carry += total;
+        __syncthreads();                            // warp_sums is reused
+    }
+    if (tid == 0) seq_start[B] = carry * upb;
+    __syncthreads();                                // the prefix is complete for every thread
+}
+
+// Position in the concatenated tile list: sequence b, unit j within the
+// sequence (kv head * head_groups + head group), tile i within the unit,
+// nb = tiles per unit of sequence b.
+struct TileCursor {
+    int b, j, i, nb;
+    __device__ __forceinline__ void seek(const int* seq_start, int B, int upb, int t) {
+        int lo = 0, hi = B - 1;                     // last b with seq_start[b] <= t
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (seq_start[mid] <= t) lo = mid; else hi = mid - 1;
+        }
+        b = lo;
+        nb = (seq_start[b + 1] - seq_start[b]) / upb;
+        const int off = t - seq_start[b];
+        j = off / nb;
+        i = off - j * nb;
+    }
+    // Moves n tiles on, n <= nb - i (never past the end of the unit); past
+    // the last sequence the cursor is left at b == B with nb = 1.
+    __device__ __forceinline__ void advance(const int* seq_start, int B, int upb, int n) {
+        i += n;
+        if (i == nb) {
+            i = 0;
+            if (++j == upb) {
+                j = 0;
+                ++b;
+                nb = b < B ? (seq_start[b + 1] - seq_start[b]) / upb : 1;
+            }
+        }
+    }
+};
+
+// CTA whose range holds tile t: the largest c with floor(c*T/C) <= t.
+__device__ __forceinline__ int cta_of_tile(long long t, long long T, long long C) {
+    return int(((t + 1) * C - 1) / T);
+}
+
+// Cross-warp fold, one 8-head tile (nt) at a time: this lane's O^T
+// fragments and its columns' (m, l) into / out of a row of the exchange area.
+template <int D, int NT>
+__device__ __forceinline__ void x_store(float* row, const float (&o)[D / 16][NT][4],
+                                        const float (&m)[NT][2], const float (&l)[NT][2], int nt) {
+#pragma unroll
+    for (int dm = 0; dm < D / 16; ++dm)
+        *reinterpret_cast<float4*>(row + dm * 4) =
+            make_float4(o[dm][nt][0], o[dm][nt][1], o[dm][nt][2], o[dm][nt][3]);
+    *reinterpret_cast<float4*>(row + (D / 16) * 4) =
+        make_float4(m[nt][0], m[nt][1], l[nt][0], l[nt][1]);
+}
+
+template <int D, int NT>
+__device__ __forceinline__ void x_fold(const float* row, float (&o)[D / 16][NT][4],
+                                       float (&m)[NT][2], float (&l)[NT][2], int nt) {
+    const float4 ml = *reinterpret_cast<const float4*>(row + (D / 16) * 4);
+    const float mo[2] = {ml.x, ml.y}, lo[2] = {ml.z, ml.w};
+    float sa[2], sb[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const float mn = fmaxf(m[nt][j], mo[j]);
+        const float mu = (mn == -INFINITY) ? 0.f : mn;
+        sa[j] = fast_exp2(m[nt][j] - mu);
+        sb[j] = fast_exp2(mo[j] - mu);
+        l[nt][j] = fmaf(l[nt][j], sa[j], lo[j] * sb[j]);
+        m[nt][j] = mn;
+    }
+#pragma unroll
+    for (int dm = 0; dm < D / 16; ++dm) {
+        const float4 v = *reinterpret_cast<const float4*>(row + dm * 4);
+        o[dm][nt][0] = fmaf(o[dm][nt][0], sa[0], v.x * sb[0]);
+        o[dm][nt][1] = fmaf(o[dm][nt][1], sa[1], v.y * sb[1]);
+        o[dm][nt][2] = fmaf(o[dm][nt][2], sa[0], v.z * sb[0]);
+        o[dm][nt][3] = fmaf(o[dm][nt][3], sa[1], v.w * sb[1]);
+    }
+}
+
+// Last piece of a unit: merges the pieces of contributors cf..cl (CTA c's
+// slot is 2c, or 2c + 1 for cf when the unit is not its first item) into the
+// fp16 output of the unit's gcount heads.  All consumer threads take part.
+// Contributors go in chunks: their (m, l) pairs are staged in shared memory
+// (one round of loads), then every thread folds its float4 quads of acc
+// with the chunk's weights, UB contributors' loads of all its quads in
+// flight at once.
+template <int D, int NT, int NW>
+__device__ __forceinline__ void merge_pieces(const DecodeParams& p, float* area, int cf, int cl,
+                                             bool cf_tail, int gcount, size_t head_base) {
+    constexpr int GP = NT * 8;
+    constexpr int NTHR = NW * 32;
+    constexpr int XFL = 2 * 32 * ((D / 16) * 4 + 4);      // floats of the exchange area
+    constexpr int KC = XFL / (2 * GP);                    // contributors per chunk
+    constexpr int QPT = (GP * D / 4 + NTHR - 1) / NTHR;   // float4 quads per thread
+    constexpr int UB = QPT <= 2 ? 8 : 2;                  // contributors per load batch
+    float* sm_m = area;                                   // [KC][GP]
+    float* sm_l = area + KC * GP;                         // [KC][GP]
+    const int tid = threadIdx.x;
+    const int nq = gcount * D / 4;
+    float4 acc[QPT];
+    float mrun[QPT], lrun[QPT];
+#pragma unroll
+    for (int i = 0; i < QPT; ++i) {
+        acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        mrun[i] = -INFINITY;
+        lrun[i] = 0.f;
+    }
+    auto slot_of = [&](int cc) { return 2 * cc + ((cc == cf && cf_tail) ? 1 : 0); };
+    const int k_all = cl - cf + 1;
+    for (int c0 = 0; c0 < k_all; c0 += KC) {
+        const int kc = min(KC, k_all - c0);
+        consumer_sync(NTHR);                              // the previous chunk is folded
+        for (int idx = tid; idx < kc * GP; idx += NTHR) {
+            const int u = idx / GP, h = idx - (idx / GP) * GP;
+            const float* pm = p.part_ml + ((size_t)slot_of(cf + c0 + u) * GP + h) * 2;
+            const bool in = h < gcount;
+            sm_m[idx] = in ? __ldcg(pm) : -INFINITY;
+            sm_l[idx] = in ? __ldcg(pm + 1) : 0.f;
+        }
+        consumer_sync(NTHR);
+        float mu[QPT];
+        int hq[QPT];
+#pragma unroll
+        for (int i = 0; i < QPT; ++i) {
+            const int q = tid + i * NTHR;
+            hq[i] = q < nq ? (q * 4) / D : 0;
+            float cm = mrun[i];
+            for (int u = 0; u < kc; ++u) cm = fmaxf(cm, sm_m[u * GP + hq[i]]);
+            mu[i] = (cm == -INFINITY) ? 0.f : cm;
+            const float r = fast_exp2(mrun[i] - mu[i]);
+            acc[i].x *= r; acc[i].y *= r; acc[i].z *= r; acc[i].w *= r;
+            lrun[i] *= r;
+            mrun[i] = cm;
+        }
+        for (int u0 = 0; u0 < kc; u0 += UB) {
+            float4 v[QPT][UB];
+#pragma unroll
+            for (int i = 0; i < QPT; ++i)
+#pragma unroll
+                for (int u = 0; u < UB; ++u) {
+                    const int q = tid + i * NTHR;
+                    const bool in = q < nq && u0 + u < kc;
+                    const float4* src = reinterpret_cast<const float4*>(
+                        p.part_acc + (size_t)slot_of(cf + c0 + u0 + u) * GP * D) + q;
+                    v[i][u] = in ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+            for (int i = 0; i < QPT; ++i)
+#pragma unroll
+                for (int u = 0; u < UB; ++u) {
+                    if (u0 + u < kc) {
+                        const float w = fast_exp2(sm_m[(u0 + u) * GP + hq[i]] - mu[i]);
+                        acc[i].x = fmaf(v[i][u].x, w, acc[i].x);
+                        acc[i].y = fmaf(v[i][u].y, w, acc[i].y);
+                        acc[i].z = fmaf(v[i][u].z, w, acc[i].z);
+                        acc[i].w = fmaf(v[i][u].w, w, acc[i].w);
+                        lrun[i] = fmaf(sm_l[(u0 + u) * GP + hq[i]], w, lrun[i]);
+                    }
+                }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < QPT; ++i) {
+        const int q = tid + i * NTHR;
+        if (q < nq) {
+            __half2* dst = reinterpret_cast<__half2*>(p.out + head_base * D + (size_t)q * 4);
+            dst[0] = __floats2half2_rn(lrun[i] > 0.f ? acc[i].x / lrun[i] : 0.f,
+                                       lrun[i] > 0.f ? acc[i].y / lrun[i] : 0.f);
+            dst[1] = __floats2half2_rn(lrun[i] > 0.f ? acc[i].z / lrun[i] : 0.f,
+                                       lrun[i] > 0.f ? acc[i].w / lrun[i] : 0.f);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent batched decode kernel.
+//   grid  = C CTAs (co-resident), block = 32 * (NW + 1): NW consumer warps +
+//   one producer warp.  p.batch sequences, p.Hkv kv heads, p.head_groups
+//   head groups of GP = 8 * NT query heads per kv head.
+//   p.counters: one per unit, zero between calls; p.part_ml / p.part_acc:
+//   2 * C partial slots of [GP][2] / [GP][D] floats.
+// ---------------------------------------------------------------------------
+template <int D, int NT, int TILE, int STAGES, int NW>
+__global__ void __launch_bounds__(32 * (NW + 1), 2)
+persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
+    static_assert(TILE == 16 * NW, "each consumer warp owns one 16-row m-tile per stage");
+    using S = PersistSmem<D, NT, TILE, STAGES, NW>;
+    constexpr int GP = NT * 8;
+    constexpr int KSTEPS = D / 16;
+    constexpr int DTILES = D / 16;
+    constexpr int XF = S::kXFloats;
+
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    unsigned char* kring = smem;
+    unsigned char* vring = smem + STAGES * S::kTileBytes;
+    float* xarea = reinterpret_cast<float*>(smem + S::kXOffset);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
+    uint64_t* empty = full + STAGES;
+    int* xflag = reinterpret_cast<int*>(smem + S::kFlagOffset);
+    int* seq_start = reinterpret_cast<int*>(smem + S::kMetaOffset);
+    int* lens = seq_start + kPersistMaxBatch + 1;
+    int* warp_sums = lens + kPersistMaxBatch;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int B = p.batch;
+    const int hg = p.head_groups;
+    const int upb = p.Hkv * hg;                     // units per sequence
+
+    grid_launch_dependents();
+    if (threadIdx.x == 0) FR_TRACE_EV(kEvStart);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NW);
+        }
+        fence_mbar_init();
+    }
+    if (!p.prefetch_meta) grid_dependency_wait();  // lengths may come from the preceding grid
+    scan_lengths<TILE>(p.kv_lens, B, upb, seq_start, lens, warp_sums);  // ends in a barrier
+
+    // C <= T CTAs take part, so every one of them owns at least one tile: the
+    // CTAs whose ranges meet a unit are exactly the ones that store a piece
+    // of it (the merge counts on that).
+    const long long T = seq_start[B];
+    const long long C = min((long long)gridDim.x, T);
+    if (blockIdx.x >= C) return;                    // uniform over the CTA
+    const int beg = int((blockIdx.x * T) / C);
+    const int end = int(((blockIdx.x + 1) * T) / C);
+    const int n = end - beg;
+    if (threadIdx.x == 0) FR_TRACE_EV(kEvMeta);
+
+    TileCursor start;
+    start.seek(seq_start, B, upb, beg);
+
+    if (warp == NW) {
+        // -------------------------------------------------------- producer
+        if (lane == 0) {
+            prefetch_tensormap(&p.kmap);
+            prefetch_tensormap(&p.vmap);
+            const uint64_t policy = p.evict_normal ? l2_policy_evict_normal() : l2_policy_evict_first();
+            bool waited = !p.prefetch_meta;
+            TileCursor cur = start;
+            int cb = cur.b;
+            long long rowb = p.row_offsets ? p.row_offsets[cb] : 0;
+            long long rown = (p.row_offsets && cb + 1 < B) ? p.row_offsets[cb + 1] : 0;
+            int issued = 0;
+            for (int k = 0; k < n; ++k) {
+                const int s = k % STAGES;
+                if (k >= STAGES && !mbar_wait_bounded(&empty[s], ((k / STAGES) - 1) & 1)) {
+                    record_error(p.err, kDevTimeoutEmpty);
+                    break;
+                }
+                if (cur.b != cb) {                  // next sequence (b grows by one)
+                    cb = cur.b;
+                    rowb = rown;
+                    rown = (p.row_offsets && cb + 1 < B) ? p.row_offsets[cb + 1] : 0;
+                }
+                // a unit's last tile holds its sequence's newest row
+                if (!waited && cur.i == cur.nb - 1) {
+                    grid_dependency_wait();
+                    waited = true;
+                }
+                const int kvh = cur.j / hg;
+                const int row = int(rowb + (long long)cur.i * TILE);
+                mbar_arrive_expect_tx(&full[s], uint32_t(2 * S::kTileBytes));
+#pragma unroll
+                for (int sub = 0; sub < S::kSub; ++sub) {
+                    tma_load_4d(kring + s * S::kTileBytes + sub * S::kSubBytes, &p.kmap, 0, sub,
+                                kvh, row, &full[s], policy);
+                    tma_load_4d(vring + s * S::kTileBytes + sub * S::kSubBytes, &p.vmap, 0, sub,
+                                kvh, row, &full[s], policy);
+                }
+                if (k == 0) FR_TRACE_EV(kEvFirstIssue);
+                ++issued;
+                cur.advance(seq_start, B, upb, 1);
+            }
+            // Drain: every copy this CTA issued has landed before it retires.
+            for (int i = max(0, issued - STAGES); i < issued; ++i) {
+                if (!mbar_wait_bounded(&full[i % STAGES], (i / STAGES) & 1)) {
+                    record_error(p.err, kDevTimeoutFull);
+                    break;
+                }
+            }
+        }
+        __syncwarp();
+        return;
+    }
+
+    // ------------------------------------------------------------ consumers
+    if (p.prefetch_meta) grid_dependency_wait();   // q and the outputs depend on it
+    if (threadIdx.x == 0) FR_TRACE_EV(kEvDepWait);
+    const int g = lane >> 2;
+    const int t = lane & 3;
+    const int row0 = warp * 16;
+    const float sl2 = p.scale_log2;
+    const uint32_t kring_s = smem_u32(kring);
+    const uint32_t vring_s = smem_u32(vring);
+    bool ok = true;
+    TileCursor cur = start;
+    int k = 0;
+    for (int e = 0; k < n; ++e) {
+        const int b = cur.b, j = cur.j, nb = cur.nb, i0 = cur.i;
+        const int cnt = min(nb - i0, n - k);
+        const int kvh = j / hg, hgrp = j - (j / hg) * hg;
+        const int h0 = kvh * p.G + hgrp * GP;
+        const int gcount = min(GP, p.G - hgrp * GP);
+        const int len = lens[b];
+        const int ustart = seq_start[b] + j * nb;  // the unit's first tile in the list
+        const size_t head_base = (size_t)b * p.H + h0;
+
+        // Q^T as the B operand of S^T = K Q^T
+        uint32_t qb[KSTEPS][NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int hj = nt * 8 + g;
+            const bool valid = hj < gcount;
+            const __half* qrow = p.q + (head_base + hj) * D;
+#pragma unroll
+            for (int ks = 0; ks < KSTEPS; ++ks) {
+                qb[ks][nt][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * t) : 0u;
+                qb[ks][nt][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * t) : 0u;
+            }
+        }
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvQLoaded);
+        float o[DTILES][NT][4];
+        float m_run[NT][2], l_run[NT][2];
+#pragma unroll
+        for (int dm = 0; dm < DTILES; ++dm)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) o[dm][nt][c] = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            m_run[nt][0] = m_run[nt][1] = -INFINITY;
+            l_run[nt][0] = l_run[nt][1] = 0.f;
+        }
+
+        for (int tt = 0; tt < cnt; ++tt, ++k) {
+            const int s = k % STAGES;
+            // After a timed-out wait the warp stops reading the ring but keeps
+            // walking the items, so every consumer barrier below still meets.
+            if (ok && !mbar_wait_bounded(&full[s], (k / STAGES) & 1)) {
+                record_error(p.err, kDevTimeoutFull);
+                ok = false;
+            }
+            if (k == 0 && threadIdx.x == 0) FR_TRACE_EV(kEvFirstFull);
+            const int tpos0 = (i0 + tt) * TILE + row0;
+            if (ok && tpos0 < len)
+                consume_tile<D, NT, TILE>(kring_s + s * S::kTileBytes, vring_s + s * S::kTileBytes,
+                                          vring + s * S::kTileBytes, row0, len - tpos0,
+                                          p.zero_tail != 0, qb, o, m_run, l_run, sl2, lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        cur.advance(seq_start, B, upb, cnt);
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvLoopEnd);
+
+        // Row sums: each lane summed its own positions; fold the 8 row groups.
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+                float l = l_run[nt][jj];
+                l += __shfl_xor_sync(0xffffffffu, l, 4);
+                l += __shfl_xor_sync(0xffffffffu, l, 8);
+                l += __shfl_xor_sync(0xffffffffu, l, 16);
+                l_run[nt][jj] = l;
+            }
+
+        // ---- cross-warp fold: warps 2,3 -> 0,1, then 1 -> 0
+        const int ok_all = consumer_sync_and(ok ? 1 : 0, NW * 32);
+        static_assert(NW == 4, "two fold rounds");
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            if (warp >= 2) x_store<D, NT>(xarea + ((warp - 2) * 32 + lane) * XF, o, m_run, l_run, nt);
+            consumer_sync(NW * 32);
+            if (warp < 2) x_fold<D, NT>(xarea + (warp * 32 + lane) * XF, o, m_run, l_run, nt);
+            consumer_sync(NW * 32);
+            if (warp == 1) x_store<D, NT>(xarea + lane * XF, o, m_run, l_run, nt);
+            consumer_sync(NW * 32);
+            if (warp == 0) x_fold<D, NT>(xarea + lane * XF, o, m_run, l_run, nt);
+            consumer_sync(NW * 32);
+        }
+
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvFold);
+        // ---- output of the item
+        const bool whole = i0 == 0 && cnt == nb;
+        if (whole) {
+            if (warp == 0 && ok_all) {
+#pragma unroll
+                for (int dm = 0; dm < DTILES; ++dm)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const int d = dm * 16 + g + ((c >> 1) << 3);
+                            const int hj = nt * 8 + 2 * t + (c & 1);
+                            const float l = l_run[nt][c & 1];
+                            if (hj < gcount)
+                                p.out[(head_base + hj) * D + d] =
+                                    __float2half_rn(l > 0.f ? o[dm][nt][c] / l : 0.f);
+                        }
+            }
+            if (threadIdx.x == 0) FR_TRACE_EV(kEvStored);
+            continue;
+        }
+        // A piece of a unit shared with other CTAs: slot 2c (first item of
+        // this CTA) or 2c + 1 (its last); a timed-out CTA stores the neutral
+        // state (m = -inf, l = 0, acc = 0).
+        const int unit = b * upb + j;
+        if (warp == 0) {
+            const int slot = 2 * blockIdx.x + (e == 0 ? 0 : 1);
+            float* pa = p.part_acc + (size_t)slot * GP * D;
+            float* pm = p.part_ml + (size_t)slot * GP * 2;
+#pragma unroll
+            for (int dm = 0; dm < DTILES; ++dm)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int d = dm * 16 + g + ((c >> 1) << 3);
+                        const int hj = nt * 8 + 2 * t + (c & 1);
+                        pa[hj * D + d] = ok_all ? o[dm][nt][c] : 0.f;
+                    }
+            if (g == 0) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int jj = 0; jj < 2; ++jj) {
+                        const int hj = nt * 8 + 2 * t + jj;
+                        pm[hj * 2 + 0] = ok_all ? m_run[nt][jj] : -INFINITY;
+                        pm[hj * 2 + 1] = ok_all ? l_run[nt][jj] : 0.f;
+                    }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                const int cf = cta_of_tile(ustart, T, C);
+                const int cl = cta_of_tile(ustart + nb - 1, T, C);
+                // acq_rel: publishes this warp's piece (ordered before by
+                // __syncwarp) and, for the last arriver, acquires the others.
+                const int old = atom_add_acq_rel_gpu(&p.counters[unit], 1);
+                const bool last = old == cl - cf;
+                if (last) p.counters[unit] = 0;         // every piece has been counted
+                xflag[0] = last ? 1 : 0;
+                xflag[1] = cf;
+                xflag[2] = cl;
+            }
+        }
+        consumer_sync(NW * 32);
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvStored);
+        if (xflag[0]) {
+            const int cf = xflag[1], cl = xflag[2];
+            const bool cf_tail = (int)((cf * T) / C) < ustart;   // the unit is cf's last item
+            merge_pieces<D, NT, NW>(p, xarea, cf, cl, cf_tail, gcount, head_base);
+            if (threadIdx.x == 0) FR_TRACE_EV(kEvMergeEnd);
+        }
+    }
+}
+
+}  // namespace fr

@@ -5,6 +5,7 @@
 // Declarations and contracts live in include/forgert_attn.h; each entry point
 // there names the reference launcher it replaces.
 #include "decode_kernels.cuh"
+#include "batched_kernels.cuh"
 #include "prefill_kernels.cuh"
 #include "prefill_tc_kernels.cuh"
 #include "rope_kernels.cuh"
@@ -55,6 +56,7 @@ struct DeviceState {
     size_t ws_bytes = 0;
     uint32_t attr_done = 0;      // bit per kernel instantiation: smem attribute set
     int occupancy[8] = {0};      // CTAs/SM per instantiation (0 = not queried)
+    int persist_occ[4] = {0};    // CTAs/SM of the persistent batched kernels
     int resident[4][5] = {{-1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1},
                           {-1, -1, -1, -1, -1}};   // co-resident clusters per (slot, log2 size)
 };
@@ -437,6 +439,146 @@ int query_resident_clusters(int D, int nt, int cl, DeviceState* st) {
     return n;
 }
 
+// ------------------------------------------------ persistent batched path
+// fr_decode_attn_batched runs the persistent stream-K kernel
+// (batched_kernels.cuh) when the batch fits its shared-memory length prefix;
+// FORGERT_BATCHED_KERNEL=split selects the split kernel's grid instead
+// (read once).  FORGERT_PERSIST_CTAS_PER_SM caps the CTAs per SM of the
+// persistent grid (default: as many as fit).
+template <int D, int NT>
+using PersistOf = fr::PersistSmem<D, NT, kTile, Stages<D>::value, kConsumerWarps>;
+
+template <int D, int NT>
+auto persist_ptr() {
+    return fr::persistent_decode_kernel<D, NT, kTile, Stages<D>::value, kConsumerWarps>;
+}
+
+bool persistent_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("FORGERT_BATCHED_KERNEL");
+        return !(v && std::strcmp(v, "split") == 0);
+    }();
+    return on;
+}
+
+int persist_ctas_per_sm(int occ) {
+    static const int cap = env_int("FORGERT_PERSIST_CTAS_PER_SM", 0);
+    return cap > 0 ? std::min(cap, occ) : occ;
+}
+
+// Attribute bits 12..15 of attr_done; occupancy in persist_occ[slot].
+template <int D, int NT>
+int prepare_persistent(DeviceState* st, int* occ) {
+    constexpr int slot = kernel_slot<D, NT>();
+    std::lock_guard<std::mutex> lk(g_prep_mu);
+    const uint32_t bit = 1u << (12 + slot);
+    if (!(st->attr_done & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(persist_ptr<D, NT>(),
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(PersistOf<D, NT>::kBytes));
+        if (e != cudaSuccess) return cuda_fail(e);
+        int n = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, persist_ptr<D, NT>(),
+                                                          32 * (kConsumerWarps + 1),
+                                                          PersistOf<D, NT>::kBytes);
+        st->persist_occ[slot] = (e == cudaSuccess && n > 0) ? n : 1;
+        st->attr_done |= bit;
+    }
+    *occ = st->persist_occ[slot];
+    return FR_OK;
+}
+
+template <int D, int NT>
+int launch_persistent(const DecodeParams& p, int ctas, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas, 1, 1);
+    cfg.blockDim = dim3(32 * (kConsumerWarps + 1), 1, 1);
+    cfg.dynamicSmemBytes = PersistOf<D, NT>::kBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, persist_ptr<D, NT>(), p);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
+
+// Grid and workspace of a persistent call: C co-resident CTAs (no more than
+// the tiles the call can have), 2 partial slots of GP x (D + 2) floats each.
+struct PersistPlan {
+    int nt = 1, head_groups = 1, ctas = 0;
+    size_t ws_bytes = 0;
+};
+
+int persistent_plan(DeviceState* st, int D, int batch, int num_kv_heads, int group,
+                    int max_kv_len, PersistPlan* pp) {
+    PersistPlan pl;
+    pl.nt = group <= 8 ? 1 : 2;
+    pl.head_groups = (group + 8 * pl.nt - 1) / (8 * pl.nt);
+    int occ = 1;
+    const int rc = D == 64 ? (pl.nt == 1 ? prepare_persistent<64, 1>(st, &occ)
+                                         : prepare_persistent<64, 2>(st, &occ))
+                           : (pl.nt == 1 ? prepare_persistent<128, 1>(st, &occ)
+                                         : prepare_persistent<128, 2>(st, &occ));
+    if (rc != FR_OK) return rc;
+    const long long upb = (long long)num_kv_heads * pl.head_groups;
+    const long long max_tiles =
+        (long long)batch * upb * std::max(1, (max_kv_len + kTile - 1) / kTile);
+    const long long slots = (long long)st->sm_count * persist_ctas_per_sm(occ);
+    pl.ctas = (int)std::max<long long>(1, std::min(slots, max_tiles));
+    const int gp = 8 * pl.nt;
+    pl.ws_bytes = kCounterBytes + (size_t)2 * pl.ctas * gp * (D + 2) * sizeof(float);
+    *pp = pl;
+    return FR_OK;
+}
+
+bool persistent_fits(int batch, int num_kv_heads, int group, int max_kv_len) {
+    if (!persistent_enabled() || batch > fr::kPersistMaxBatch) return false;
+    const int nt = group <= 8 ? 1 : 2;
+    const long long upb = (long long)num_kv_heads * ((group + 8 * nt - 1) / (8 * nt));
+    const long long units = (long long)batch * upb;
+    const long long tiles = units * std::max(1, (max_kv_len + kTile - 1) / kTile);
+    return units <= kMaxUnits && tiles < (1LL << 30);
+}
+
+int run_persistent(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* out,
+                   cudaStream_t s) {
+    DeviceState* st = nullptr;
+    int rc = get_state(&st);
+    if (rc != FR_OK) return rc;
+    const int group = p.H / p.Hkv;
+    PersistPlan pl;
+    rc = persistent_plan(st, head_dim, batch, p.Hkv, group, max_kv_len, &pl);
+    if (rc != FR_OK) return rc;
+    rc = ensure_workspace(st, pl.ws_bytes, s);
+    if (rc != FR_OK) return rc;
+    p.G = group;
+    p.head_groups = pl.head_groups;
+    p.batch = batch;
+    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+    p.err = st->err;
+    p.out = out;
+    p.counters = static_cast<int*>(st->ws);
+    p.part_ml = reinterpret_cast<float*>(static_cast<char*>(st->ws) + kCounterBytes);
+    p.part_acc = p.part_ml + (size_t)2 * pl.ctas * 8 * pl.nt * 2;
+    static const int evict_normal = env_int("FORGERT_EVICT_NORMAL", 0);
+    p.evict_normal = evict_normal;
+    const bool pdl = s != nullptr;
+    p.prefetch_meta = (pdl && g_overlap.load(std::memory_order_relaxed)) ? 1 : 0;
+    static const int trace_plan = env_int("FORGERT_TRACE_PLAN", 0);
+    if (trace_plan)
+        std::fprintf(stderr, "[forgert] persistent D=%d batch=%d units=%d ctas=%d prefetch=%d\n",
+                     head_dim, batch, batch * p.Hkv * pl.head_groups, pl.ctas, p.prefetch_meta);
+    if (head_dim == 64)
+        return pl.nt == 1 ? launch_persistent<64, 1>(p, pl.ctas, s, pdl)
+                          : launch_persistent<64, 2>(p, pl.ctas, s, pdl);
+    return pl.nt == 1 ? launch_persistent<128, 1>(p, pl.ctas, s, pdl)
+                      : launch_persistent<128, 2>(p, pl.ctas, s, pdl);
+}
+
 // Shared driver of the decode-family entry points.  `p` carries the tensor
 // maps and the sequence geometry.
 //   final_out != nullptr : write fp16 output
@@ -787,6 +929,9 @@ int fr_decode_attn_batched(const void* q, const void* k_pool, const void* v_pool
     p.row_offsets = row_offsets;
     p.kv_lens = kv_lens;
     p.zero_tail = 1;
+    if (persistent_fits(batch, num_kv_heads, num_heads / num_kv_heads, std::max(1, max_kv_len)))
+        return run_persistent(p, head_dim, batch, std::max(1, max_kv_len),
+                              static_cast<__half*>(out), static_cast<cudaStream_t>(stream));
     return run_decode(p, head_dim, batch, std::max(1, max_kv_len), static_cast<__half*>(out),
                       nullptr, nullptr, batch_waves(), static_cast<cudaStream_t>(stream));
 }
@@ -1069,7 +1214,15 @@ size_t fr_decode_workspace_size(int batch, int num_heads, int num_kv_heads, int 
             FR_OK)
         return 0;
     const int splits = std::max(pl1.num_splits, pl4.num_splits) + kClusterCtas;
-    return kCounterBytes + partial_bytes((long long)batch * num_heads, splits, head_dim);
+    size_t need = kCounterBytes + partial_bytes((long long)batch * num_heads, splits, head_dim);
+    if (persistent_fits(batch, num_kv_heads, group, std::max(1, max_kv_len))) {
+        PersistPlan pp;
+        if (persistent_plan(st, head_dim, batch, num_kv_heads, group, std::max(1, max_kv_len),
+                            &pp) != FR_OK)
+            return 0;
+        need = std::max(need, pp.ws_bytes);
+    }
+    return need;
 }
 
 size_t fr_prefill_workspace_size(int seq_len, int num_heads, int head_dim) {
@@ -1209,6 +1362,29 @@ int fr_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
 }
 
 unsigned long long fr_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+#ifdef FR_TRACE
+// Trace builds only (libforgert_b200_trace.so): attach a device buffer of
+// kTraceMaxCtas x kTracePerCta fr::TraceRec records (nullptr detaches),
+// zeroing the per-CTA launch and record counters; fr_trace_fill copies the
+// kTraceMaxCtas record counts to host memory.
+FR_API int fr_trace_attach(void* buf) {
+    void* a = nullptr;
+    void* b = nullptr;
+    cudaError_t e = cudaMemcpyToSymbol(fr::fr_trace_buf, &buf, sizeof(buf));
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&a, fr::fr_trace_launch);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&b, fr::fr_trace_fill);
+    if (e == cudaSuccess) e = cudaMemset(a, 0, sizeof(unsigned) * fr::kTraceMaxCtas);
+    if (e == cudaSuccess) e = cudaMemset(b, 0, sizeof(unsigned) * fr::kTraceMaxCtas);
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
+
+FR_API int fr_trace_fill(unsigned* host_counts) {
+    cudaError_t e = cudaMemcpyFromSymbol(host_counts, fr::fr_trace_fill,
+                                         sizeof(unsigned) * fr::kTraceMaxCtas);
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
+#endif
 
 }  // extern "C"
 

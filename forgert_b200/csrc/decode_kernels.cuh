@@ -38,6 +38,7 @@
 // separate-launch form of the same merge.
 #pragma once
 #include "fr_ptx.cuh"
+#include "trace.cuh"
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -74,6 +75,11 @@ struct DecodeParams {
                                  // between calls; nullptr = unfused (lse_merge_kernel follows)
     int* err;                    // device error word
     int evict_normal;            // 1: K/V loads without the L2 evict-first hint
+    // Persistent batched kernel (batched_kernels.cuh): sequences of the call
+    // and whether lengths, row offsets and all but each unit's last tile may
+    // be read before the grid-dependency wait.
+    int batch;
+    int prefetch_meta;
     // Paged KV (kernel instantiated with PAGED): the tensor maps view the page
     // pool [num_pages * page_size rows][Hkv][D/64][64]; logical position t of
     // sequence b is row block_table[b * bt_stride + t / page_size] * page_size
@@ -200,6 +206,125 @@ __device__ __forceinline__ uint32_t swz_offset(int r, int col) {
 }
 
 // ---------------------------------------------------------------------------
+// One consumer warp's share of one K/V tile: rows row0 .. row0 + 15 of the
+// stage at kst / vst (shared-memory addresses; vgen = the V stage's generic
+// address), of which the first valid_rows (>= 1) are real positions.
+//   S^T = K Q^T (16 positions x GP heads), masked past valid_rows;
+//   online softmax per head column in base 2 (m_run, l_run: this lane's
+//   running max and partial row sum; o: the warp's O^T fragments);
+//   O^T += V^T P^T with P = P_hi + P_lo (two fp16 halves).
+// zero_tail: rows past the end may hold non-finite data (another
+// sequence's rows of a pool); they are zeroed in V so P = 0 multiplies
+// finite values.
+// ---------------------------------------------------------------------------
+template <int D, int NT, int TILE>
+__device__ __forceinline__ void consume_tile(uint32_t kst, uint32_t vst, unsigned char* vgen,
+                                             int row0, int valid_rows, bool zero_tail,
+                                             const uint32_t (&qb)[D / 16][NT][2],
+                                             float (&o)[D / 16][NT][4], float (&m_run)[NT][2],
+                                             float (&l_run)[NT][2], float sl2, int lane) {
+    constexpr int KSTEPS = D / 16;
+    constexpr int DTILES = D / 16;
+    constexpr int kSub = D / 64;
+    constexpr int kSubBytes = TILE * 128;
+    const int g = lane >> 2;
+    // ldmatrix rows/columns of this lane (see the fragment maps in the file header).
+    const int k_row = row0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+    const int k_col = (lane >> 4) * 8;
+    const int v_row = row0 + (lane & 7) + ((lane >> 4) & 1) * 8;
+    const int v_col = ((lane >> 3) & 1) * 8;
+    bool fenced = false;
+    if (zero_tail && valid_rows < 16) {
+        for (int c = lane; c < (16 - valid_rows) * kSub * 8; c += 32) {
+            const int r = row0 + valid_rows + c / (kSub * 8);
+            const int rest = c % (kSub * 8);
+            *reinterpret_cast<uint4*>(vgen + (rest >> 3) * kSubBytes + r * 128 + (rest & 7) * 16) =
+                make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+        fenced = true;
+    }
+
+    // ---- S^T = K Q^T (16 positions x GP heads)
+    float sacc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(a0, a1, a2, a3, kst + swz_offset<TILE>(k_row, ks * 16 + k_col));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            mma_16816(sacc[nt], a0, a1, a2, a3, qb[ks][nt][0], qb[ks][nt][1]);
+    }
+
+    // ---- mask rows past the end
+    const bool row_lo_ok = g < valid_rows;
+    const bool row_hi_ok = g + 8 < valid_rows;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        if (!row_lo_ok) { sacc[nt][0] = -INFINITY; sacc[nt][1] = -INFINITY; }
+        if (!row_hi_ok) { sacc[nt][2] = -INFINITY; sacc[nt][3] = -INFINITY; }
+    }
+
+    // ---- online softmax per head column (base 2)
+    uint32_t pb[NT][2];
+    uint32_t pl[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        float alpha[2];
+        float pr[4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            float mx = fmaxf(sacc[nt][j], sacc[nt][j + 2]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float m_new = fmaxf(m_run[nt][j], mx * sl2);
+            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+            alpha[j] = fast_exp2(m_run[nt][j] - m_use);
+            m_run[nt][j] = m_new;
+            pr[j] = fast_exp2(fmaf(sacc[nt][j], sl2, -m_use));
+            pr[j + 2] = fast_exp2(fmaf(sacc[nt][j + 2], sl2, -m_use));
+            l_run[nt][j] = fmaf(l_run[nt][j], alpha[j], pr[j] + pr[j + 2]);
+        }
+#pragma unroll
+        for (int dm = 0; dm < DTILES; ++dm) {
+            o[dm][nt][0] *= alpha[0];
+            o[dm][nt][1] *= alpha[1];
+            o[dm][nt][2] *= alpha[0];
+            o[dm][nt][3] *= alpha[1];
+        }
+        // P^T fragments: rows = positions, cols = heads -> B layout
+        // (k = pos, n = head).  P = P_hi + P_lo, both fp16.
+        const __half2 h01 = __floats2half2_rn(pr[0], pr[1]);
+        const __half2 h23 = __floats2half2_rn(pr[2], pr[3]);
+        pb[nt][0] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h01));
+        pb[nt][1] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h23));
+        const float2 f01 = __half22float2(h01);
+        const float2 f23 = __half22float2(h23);
+        pl[nt][0] = movmatrix_trans(pack_half2(pr[0] - f01.x, pr[1] - f01.y));
+        pl[nt][1] = movmatrix_trans(pack_half2(pr[2] - f23.x, pr[3] - f23.y));
+    }
+
+    // ---- O^T += V^T P^T
+#pragma unroll
+    for (int dm = 0; dm < DTILES; ++dm) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_trans(a0, a1, a2, a3, vst + swz_offset<TILE>(v_row, dm * 16 + v_col));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            mma_16816(o[dm][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+            mma_16816(o[dm][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+        }
+    }
+    // Generic-proxy writes into a stage the TMA will refill later.
+    if (fenced) fence_proxy_async_smem();
+}
+
+// ---------------------------------------------------------------------------
 // Split-KV decode kernel.
 //   grid  = (Hkv * head_groups, num_splits, B), clusters of CL CTAs along y
 //   block = 32 * (NW + 1): NW consumer warps + 1 producer warp
@@ -231,7 +356,6 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     constexpr int GP = NT * 8;          // padded heads per CTA
     constexpr int KSTEPS = D / 16;      // k-steps of the QK product
     constexpr int DTILES = D / 16;      // m-tiles of the PV product
-    constexpr bool kSplitP = true;      // hi/lo fp16 split of P (fp32-grade P.V)
 
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -268,6 +392,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
 
     // Every CTA of this grid is running: the next grid may start launching.
     grid_launch_dependents();
+    if (threadIdx.x == 0) FR_TRACE_EV(kEvStart);
 
     // Fused merge across a cluster: every CTA pushes each peer its (m, l) and
     // that peer's slice of acc (st.async into the peer's receive area, bytes
@@ -399,6 +524,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                     tma_load_4d(vring + s * S::kTileBytes + sub * S::kSubBytes, &p.vmap, 0, sub,
                                 kvh, row, &full[s], policy);
                 }
+                if (i == 0) FR_TRACE_EV(kEvFirstIssue);
                 ++issued;
             }
             // Drain: wait until every copy this CTA issued has landed, so no
@@ -416,6 +542,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         // -------------------------------------------------------- consumers
         // q (and everything this CTA writes) depends on the preceding grid.
         grid_dependency_wait();
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvDepWait);
 
         // Q^T as the B operand of S^T = K Q^T: b0 = Q[head][ks*16 + 2t .. +1], b1 = +8.
         uint32_t qb[KSTEPS][NT][2];
@@ -434,6 +561,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
             }
         }
 
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvQLoaded);
 #pragma unroll
         for (int dm = 0; dm < DTILES; ++dm)
 #pragma unroll
@@ -447,12 +575,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         }
 
         const float sl2 = p.scale_log2;
-        // ldmatrix rows/columns of this lane (see the fragment maps in the file header).
-        const int row0 = warp * 16;
-        const int k_row = row0 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int k_col = (lane >> 4) * 8;
-        const int v_row = row0 + (lane & 7) + ((lane >> 4) & 1) * 8;
-        const int v_col = ((lane >> 3) & 1) * 8;
+        const int row0 = warp * 16;          // this warp's 16 rows of every tile
         const uint32_t kring_s = smem_u32(kring);
         const uint32_t vring_s = smem_u32(vring);
 
@@ -463,107 +586,12 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                 ok = false;
                 break;
             }
+            if (i == 0 && threadIdx.x == 0) FR_TRACE_EV(kEvFirstFull);
             const int tpos0 = pos_begin + i * TILE + row0;     // first position of this warp's m-tile
-            if (tpos0 < pos_end) {
-                const uint32_t kst = kring_s + s * S::kTileBytes;
-                const uint32_t vst = vring_s + s * S::kTileBytes;
-                const int valid_rows = pos_end - tpos0;        // rows >= this are past the end
-                bool fenced = false;
-                if (p.zero_tail && valid_rows < 16) {
-                    // Rows past the sequence may hold anything (other sequences'
-                    // rows of a pool); zero this warp's V rows there so that
-                    // P = 0 multiplies finite values.
-                    unsigned char* vbase = vring + s * S::kTileBytes;
-                    for (int c = lane; c < (16 - valid_rows) * S::kSub * 8; c += 32) {
-                        const int r = row0 + valid_rows + c / (S::kSub * 8);
-                        const int rest = c % (S::kSub * 8);
-                        *reinterpret_cast<uint4*>(vbase + (rest >> 3) * S::kSubBytes + r * 128 +
-                                                  (rest & 7) * 16) = make_uint4(0, 0, 0, 0);
-                    }
-                    __syncwarp();
-                    fenced = true;
-                }
-
-                // ---- S^T = K Q^T (16 positions x GP heads)
-                float sacc[NT][4];
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
-#pragma unroll
-                for (int ks = 0; ks < KSTEPS; ++ks) {
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4(a0, a1, a2, a3, kst + swz_offset<TILE>(k_row, ks * 16 + k_col));
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-                        mma_16816(sacc[nt], a0, a1, a2, a3, qb[ks][nt][0], qb[ks][nt][1]);
-                }
-
-                // ---- mask rows past the end of the split
-                const bool row_lo_ok = g < valid_rows;
-                const bool row_hi_ok = g + 8 < valid_rows;
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    if (!row_lo_ok) { sacc[nt][0] = -INFINITY; sacc[nt][1] = -INFINITY; }
-                    if (!row_hi_ok) { sacc[nt][2] = -INFINITY; sacc[nt][3] = -INFINITY; }
-                }
-
-                // ---- online softmax per head column (base 2)
-                uint32_t pb[NT][2];
-                uint32_t pl[NT][2];
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    float alpha[2];
-                    float pr[4];
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        float mx = fmaxf(sacc[nt][j], sacc[nt][j + 2]);
-                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                        const float m_new = fmaxf(m_run[nt][j], mx * sl2);
-                        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-                        alpha[j] = fast_exp2(m_run[nt][j] - m_use);
-                        m_run[nt][j] = m_new;
-                        pr[j] = fast_exp2(fmaf(sacc[nt][j], sl2, -m_use));
-                        pr[j + 2] = fast_exp2(fmaf(sacc[nt][j + 2], sl2, -m_use));
-                        l_run[nt][j] = fmaf(l_run[nt][j], alpha[j], pr[j] + pr[j + 2]);
-                    }
-#pragma unroll
-                    for (int dm = 0; dm < DTILES; ++dm) {
-                        o[dm][nt][0] *= alpha[0];
-                        o[dm][nt][1] *= alpha[1];
-                        o[dm][nt][2] *= alpha[0];
-                        o[dm][nt][3] *= alpha[1];
-                    }
-                    // P^T fragments: rows = positions, cols = heads -> B layout
-                    // (k = pos, n = head).  P = P_hi + P_lo, both fp16.
-                    const __half2 h01 = __floats2half2_rn(pr[0], pr[1]);
-                    const __half2 h23 = __floats2half2_rn(pr[2], pr[3]);
-                    pb[nt][0] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h01));
-                    pb[nt][1] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&h23));
-                    if (kSplitP) {
-                        const float2 f01 = __half22float2(h01);
-                        const float2 f23 = __half22float2(h23);
-                        pl[nt][0] = movmatrix_trans(pack_half2(pr[0] - f01.x, pr[1] - f01.y));
-                        pl[nt][1] = movmatrix_trans(pack_half2(pr[2] - f23.x, pr[3] - f23.y));
-                    }
-                }
-
-                // ---- O^T += V^T P^T
-#pragma unroll
-                for (int dm = 0; dm < DTILES; ++dm) {
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4_trans(a0, a1, a2, a3, vst + swz_offset<TILE>(v_row, dm * 16 + v_col));
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        mma_16816(o[dm][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
-                        if (kSplitP) mma_16816(o[dm][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
-                    }
-                }
-                // Generic-proxy writes into a stage the TMA will refill later.
-                if (fenced) fence_proxy_async_smem();
-            }
+            if (tpos0 < pos_end)
+                consume_tile<D, NT, TILE>(kring_s + s * S::kTileBytes, vring_s + s * S::kTileBytes,
+                                          vring + s * S::kTileBytes, row0, pos_end - tpos0,
+                                          p.zero_tail != 0, qb, o, m_run, l_run, sl2, lane);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
@@ -580,6 +608,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                 l_run[nt][j] = l;
             }
 
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvLoopEnd);
         // Every consumer must be past its last ldmatrix before the ring is
         // reused as the merge area.
         const int ok_all = consumer_sync_and(ok ? 1 : 0, NW * 32);
@@ -671,6 +700,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         }
     }
 
+    if (threadIdx.x == 0) FR_TRACE_EV(kEvFold);
     if (!p.counters) return;       // unfused / single-split paths end here (uniform)
     __syncthreads();               // CTA state complete (producer included)
 
@@ -780,6 +810,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
             }
         }
     }
+    if (threadIdx.x == 0) FR_TRACE_EV(kEvMergeEnd);
     if (ncl > 1) {
         __syncthreads();                             // slice stores of this CTA are done
         if (threadIdx.x == 0) {
@@ -833,6 +864,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                 }
             }
             if (threadIdx.x == 0) p.counters[unit * CL + crank] = 0;   // ready for the next call
+            if (threadIdx.x == 0) FR_TRACE_EV(kEvXMergeEnd);
         }
     }
 

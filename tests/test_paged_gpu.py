@@ -6,9 +6,9 @@ sequence owns with NaN, and compares the fp16 output with
 
 * the CPU oracle (oracle.paged_f64: rows gathered back into one cache per
   sequence, fp64) at max |x - r| <= 2e-3 and max |x - r| / max(|r|, 1e-3) <= 1e-2;
-* the contiguous-pool batched call on the same sequences, bit for bit: the
-  paged and pooled layouts share the split plan and the arithmetic, only the
-  address of each 16..64-row box differs.
+* the contiguous-pool batched call on the same sequences, at the same
+  tolerance (the pooled layout runs the persistent batched kernel, which
+  splits the rows differently).
 """
 from __future__ import annotations
 
@@ -64,9 +64,10 @@ def test_paged_matches_oracle_and_pool(page_size, D, H, Hkv):
     ref = O.paged_f64(q, kp, vp, table, lens, page_size)
     assert_close(out, ref, what=f"paged page_size={page_size} D={D}")
     assert np.all(out[4] == 0), "kv_len 0 yields zeros"
+    # The pooled layout runs the persistent batched kernel (a different split
+    # of the same rows), so the two agree to the tolerance, not bit for bit.
     pooled = run_batched(q, ks, vs, lens, gap_rows=3)
-    assert np.array_equal(out.view(np.uint16), pooled.view(np.uint16)), \
-        "paged and pooled layouts differ"
+    assert_close(out, pooled, what=f"paged vs pooled page_size={page_size} D={D}")
 
 
 def test_paged_out_of_pool_ids_read_as_zero_rows():
