@@ -335,8 +335,13 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
     // C <= T CTAs take part, so every one of them owns at least one tile: the
     // CTAs whose ranges meet a unit are exactly the ones that store a piece
     // of it (the merge counts on that).
+    // Few tiles per CTA: fewer CTAs, each with a longer range (its fixed
+    // costs - first tile, fold, piece store - weigh less, and the freed SM
+    // slots let the next launch's CTAs start early).
     const long long T = seq_start[B];
-    const long long C = min((long long)gridDim.x, T);
+    long long C = min((long long)gridDim.x, T);
+    if (p.min_tiles_per_cta > 0)
+        C = min(C, max((long long)p.min_ctas, T / p.min_tiles_per_cta));
     if (blockIdx.x >= C) return;                    // uniform over the CTA
     const int beg = int((blockIdx.x * T) / C);
     const int end = int(((blockIdx.x + 1) * T) / C);

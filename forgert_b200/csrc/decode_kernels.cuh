@@ -80,6 +80,10 @@ struct DecodeParams {
     // be read before the grid-dependency wait.
     int batch;
     int prefetch_meta;
+    // The persistent grid uses only as many CTAs as give each at least
+    // min_tiles_per_cta tiles, never fewer than min_ctas (0 = all of them).
+    int min_tiles_per_cta;
+    int min_ctas;
     // Paged KV (kernel instantiated with PAGED): the tensor maps view the page
     // pool [num_pages * page_size rows][Hkv][D/64][64]; logical position t of
     // sequence b is row block_table[b * bt_stride + t / page_size] * page_size
@@ -383,7 +387,10 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     const int h0 = kvh * p.G + hgrp * GP;
     const int gcount = min(GP, p.G - hgrp * GP);
 
-    // Sequence geometry.
+    // Sequence geometry.  A batch's lengths and row offsets may come from the
+    // preceding kernel: read them after its completion unless the caller
+    // declared them stable (prefetch_meta, launch overlap).
+    if (p.kv_lens && !p.prefetch_meta) grid_dependency_wait();
     const int seq_len = p.kv_lens ? p.kv_lens[b] : p.kv_len;
     const long long row_base = p.row_offsets ? p.row_offsets[b] : 0;
     const int pos_begin = split * p.split_len;
