@@ -5,26 +5,31 @@
 // softmax.  (The reference decodes one sequence per call,
 // kernels/attention_decode.cu:535-556; batching is this library's addition.)
 //
-// Work decomposition (stream-K over K/V tiles).  Every unit is cut into
-// 64-row tiles (at least one, so a zero-length sequence still yields zeros).
-// Concatenating all units' tiles in (sequence, kv head, head group) order
-// gives T tiles; the grid is persistent - C CTAs, as many as are co-resident
-// - and CTA c takes the contiguous tile range [c*T/C, (c+1)*T/C).  Every CTA
-// therefore streams the same number of K/V bytes (within one tile) whatever
-// the length distribution, and no CTA is launched without work.  A CTA's
-// range is a sequence of "items" (the tiles of one unit inside the range):
-// items in the middle of the range cover a whole unit; only the first and the
-// last item can be a piece of a unit that other CTAs share.
+// Work decomposition (cost-balanced stream-K over K/V tiles).  Every unit
+// is cut into 64-row tiles (at least one, so a zero-length sequence still
+// yields zeros).  Concatenating all units' tiles in (sequence, kv head, head
+// group) order gives T tiles; each unit is also charged a fixed cost before
+// its first tile (starting an item) and after its last (its merge), in tile
+// times (CostMap).  The grid is persistent - as many CTAs as are co-resident,
+// fewer when that would leave under min_tiles_per_cta tiles each - and CTA c
+// takes the c-th equal share of the total cost: every CTA is busy for the
+// same time whatever the length distribution and wherever unit boundaries
+// fall, and no CTA is launched without work.  A CTA's range is a sequence of
+// "items" (the tiles of one unit inside the range): items in the middle of
+// the range cover a whole unit; only the first and the last item can be a
+// piece of a unit that other CTAs share.
 //
 // Per item: the consumer warps keep the split kernel's per-warp online
-// softmax (consume_tile, decode_kernels.cuh), fold their four states through
-// a small shared-memory exchange area in two rounds (warps 2,3 -> 0,1 ->
-// 0), and warp 0 either writes the normalised fp16 output (whole unit) or
-// stores the piece's (m, l, acc) state in the CTA's partial slot (2c for its
-// first item, 2c + 1 for its last) and counts it on the unit's counter; the
-// CTA whose count completes the unit merges every piece (log-sum-exp) into
-// the output and re-arms the counter.  Meanwhile the producer warp keeps
-// streaming the next item's tiles through the TMA ring: the ring never
+// softmax (consume_tile, decode_kernels.cuh) and fold their four states
+// through a small shared-memory exchange area in two rounds (warps 2,3 ->
+// 0,1 -> 0).  Warp 0 then writes the normalised fp16 output (whole unit) or
+// stores the piece's (m, l, acc) state in the CTA's partial slot (2c for
+// its first item, 2c + 1 for its last) and counts it on the unit's counter.
+// The CTA holding a unit's last tile merges the unit after its own range
+// (bounded wait until every piece is counted, log-sum-exp merge, re-arm);
+// all CTAs of the grid are resident by then, since the next grid can launch
+// only once every CTA of this one has started.  Meanwhile the producer warp
+// keeps streaming the next item's tiles through the TMA ring: the ring never
 // drains at item boundaries.
 //
 // Metadata: every CTA reads kv_lens (B <= kPersistMaxBatch) and forms the
@@ -146,10 +151,48 @@ struct TileCursor {
     }
 };
 
-// CTA whose range holds tile t: the largest c with floor(c*T/C) <= t.
-__device__ __forceinline__ int cta_of_tile(long long t, long long T, long long C) {
-    return int(((t + 1) * C - 1) / T);
-}
+// Cost-balanced partition.  Every unit costs its tiles plus `xc` tile-times
+// placed before its first tile (starting an item: q load, and the fold and
+// piece store of the item it ends) and `mc` after its last tile (its merge,
+// done by the CTA holding that tile).  In cost space unit j of sequence b
+// spans xc + nb + mc points from cs(b) + j * (nb + xc + mc), the sequence's
+// cost start being cs(b) = seq_start[b] + (xc + mc) * upb * b.  CTA c owns
+// the cost range [c*Ctot/C, (c+1)*Ctot/C);
+// its tiles are those whose cost points fall in it (the unit's first tile
+// also owns the xc points before it, its last tile the mc points after it).
+// With Ctot / C >= xc + mc + 2 every CTA owns at least one tile.
+struct CostMap {
+    const int* seq_start;
+    int B, upb, xc, mc;
+    long long Ctot, C;
+
+    __device__ __forceinline__ long long cs(int b) const {
+        return seq_start[b] + (long long)(xc + mc) * upb * b;
+    }
+    // first tile whose cost points reach v (v < Ctot)
+    __device__ __forceinline__ int tile_at(long long v) const {
+        int lo = 0, hi = B - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (cs(mid) <= v) lo = mid; else hi = mid - 1;
+        }
+        const int nb = (seq_start[lo + 1] - seq_start[lo]) / upb;
+        const long long span = nb + xc + mc;
+        const long long off = v - cs(lo);
+        const int j = (int)min(off / span, (long long)(upb - 1));
+        const long long r = off - j * span;
+        const int i = (int)max(0LL, min(r - xc, (long long)(nb - 1)));
+        return seq_start[lo] + j * nb + i;
+    }
+    __device__ __forceinline__ int beg(long long c) const {
+        return c >= C ? seq_start[B] : tile_at((c * Ctot) / C);
+    }
+    // CTA owning the last cost point of tile i of unit j of sequence b
+    __device__ __forceinline__ int cta_of(int b, int j, int nb, int i) const {
+        const long long hi = cs(b) + (long long)j * (nb + xc + mc) + xc + i + (i == nb - 1 ? mc : 0);
+        return int(((hi + 1) * C - 1) / Ctot);
+    }
+};
 
 // Cross-warp fold, one 8-head tile (nt) at a time: this lane's O^T
 // fragments and its columns' (m, l) into / out of a row of the exchange area.
@@ -189,33 +232,40 @@ __device__ __forceinline__ void x_fold(const float* row, float (&o)[D / 16][NT][
     }
 }
 
-// Last piece of a unit: merges the pieces of contributors cf..cl (CTA c's
-// slot is 2c, or 2c + 1 for cf when the unit is not its first item) into the
-// fp16 output of the unit's gcount heads.  All consumer threads take part.
-// Contributors go in chunks: their (m, l) pairs are staged in shared memory
-// (one round of loads), then every thread folds its float4 quads of acc
-// with the chunk's weights, UB contributors' loads of all its quads in
-// flight at once.
+// Merges the pieces of a unit, stored by contributors cf..cl (CTA c's slot is
+// 2c, or 2c + 1 for cf when the unit is not its first item), into the fp16
+// output of the unit's gcount heads.  Pieces are kept in the consumer
+// fragment order - slot [dm][nt][lane] float4 = o[dm][nt][0..3] of that
+// lane, then (m, l) per head - so every thread folds whole float4
+// fragments: fragment f = (dm, nt, lane) holds heads nt*8 + 2(lane&3) +
+// {0,1} at dims dm*16 + lane/4 + {0,8}.  Contributors go in chunks: their
+// (m, l) pairs are staged in shared memory with one round of loads, then
+// each thread folds its fragments with UB contributors' loads in flight.
+// All consumer threads take part.
 template <int D, int NT, int NW>
 __device__ __forceinline__ void merge_pieces(const DecodeParams& p, float* area, int cf, int cl,
                                              bool cf_tail, int gcount, size_t head_base) {
     constexpr int GP = NT * 8;
+    constexpr int DTILES = D / 16;
     constexpr int NTHR = NW * 32;
     constexpr int XFL = 2 * 32 * ((D / 16) * 4 + 4);      // floats of the exchange area
     constexpr int KC = XFL / (2 * GP);                    // contributors per chunk
-    constexpr int QPT = (GP * D / 4 + NTHR - 1) / NTHR;   // float4 quads per thread
-    constexpr int UB = QPT <= 2 ? 8 : 2;                  // contributors per load batch
+    constexpr int NFRAG = DTILES * NT * 32;               // float4 fragments per piece
+    constexpr int FPT = (NFRAG + NTHR - 1) / NTHR;        // fragments per thread
+    constexpr int UB = FPT <= 2 ? 8 : 2;                  // contributors per load batch
     float* sm_m = area;                                   // [KC][GP]
     float* sm_l = area + KC * GP;                         // [KC][GP]
     const int tid = threadIdx.x;
-    const int nq = gcount * D / 4;
-    float4 acc[QPT];
-    float mrun[QPT], lrun[QPT];
+    float4 acc[FPT];
+    float mrun[FPT][2], lrun[FPT][2];
+    int ha[FPT];                                          // first head of the fragment
 #pragma unroll
-    for (int i = 0; i < QPT; ++i) {
+    for (int i = 0; i < FPT; ++i) {
         acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        mrun[i] = -INFINITY;
-        lrun[i] = 0.f;
+        mrun[i][0] = mrun[i][1] = -INFINITY;
+        lrun[i][0] = lrun[i][1] = 0.f;
+        const int f = tid + i * NTHR;
+        ha[i] = ((f >> 5) % NT) * 8 + 2 * (f & 3);
     }
     auto slot_of = [&](int cc) { return 2 * cc + ((cc == cf && cf_tail) ? 1 : 0); };
     const int k_all = cl - cf + 1;
@@ -225,61 +275,67 @@ __device__ __forceinline__ void merge_pieces(const DecodeParams& p, float* area,
         for (int idx = tid; idx < kc * GP; idx += NTHR) {
             const int u = idx / GP, h = idx - (idx / GP) * GP;
             const float* pm = p.part_ml + ((size_t)slot_of(cf + c0 + u) * GP + h) * 2;
-            const bool in = h < gcount;
-            sm_m[idx] = in ? __ldcg(pm) : -INFINITY;
-            sm_l[idx] = in ? __ldcg(pm + 1) : 0.f;
+            sm_m[idx] = __ldcg(pm);
+            sm_l[idx] = __ldcg(pm + 1);
         }
         consumer_sync(NTHR);
-        float mu[QPT];
-        int hq[QPT];
+        float mu[FPT][2];
 #pragma unroll
-        for (int i = 0; i < QPT; ++i) {
-            const int q = tid + i * NTHR;
-            hq[i] = q < nq ? (q * 4) / D : 0;
-            float cm = mrun[i];
-            for (int u = 0; u < kc; ++u) cm = fmaxf(cm, sm_m[u * GP + hq[i]]);
-            mu[i] = (cm == -INFINITY) ? 0.f : cm;
-            const float r = fast_exp2(mrun[i] - mu[i]);
-            acc[i].x *= r; acc[i].y *= r; acc[i].z *= r; acc[i].w *= r;
-            lrun[i] *= r;
-            mrun[i] = cm;
-        }
+        for (int i = 0; i < FPT; ++i)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                float cm = mrun[i][j];
+                for (int u = 0; u < kc; ++u) cm = fmaxf(cm, sm_m[u * GP + ha[i] + j]);
+                mu[i][j] = (cm == -INFINITY) ? 0.f : cm;
+                const float r = fast_exp2(mrun[i][j] - mu[i][j]);
+                lrun[i][j] *= r;
+                if (j == 0) { acc[i].x *= r; acc[i].z *= r; } else { acc[i].y *= r; acc[i].w *= r; }
+                mrun[i][j] = cm;
+            }
         for (int u0 = 0; u0 < kc; u0 += UB) {
-            float4 v[QPT][UB];
+            float4 v[FPT][UB];
 #pragma unroll
-            for (int i = 0; i < QPT; ++i)
+            for (int i = 0; i < FPT; ++i)
 #pragma unroll
                 for (int u = 0; u < UB; ++u) {
-                    const int q = tid + i * NTHR;
-                    const bool in = q < nq && u0 + u < kc;
+                    const int f = tid + i * NTHR;
+                    const bool in = f < NFRAG && u0 + u < kc;
                     const float4* src = reinterpret_cast<const float4*>(
-                        p.part_acc + (size_t)slot_of(cf + c0 + u0 + u) * GP * D) + q;
+                        p.part_acc + (size_t)slot_of(cf + c0 + u0 + u) * GP * D) + f;
                     v[i][u] = in ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
-            for (int i = 0; i < QPT; ++i)
+            for (int i = 0; i < FPT; ++i)
 #pragma unroll
                 for (int u = 0; u < UB; ++u) {
                     if (u0 + u < kc) {
-                        const float w = fast_exp2(sm_m[(u0 + u) * GP + hq[i]] - mu[i]);
-                        acc[i].x = fmaf(v[i][u].x, w, acc[i].x);
-                        acc[i].y = fmaf(v[i][u].y, w, acc[i].y);
-                        acc[i].z = fmaf(v[i][u].z, w, acc[i].z);
-                        acc[i].w = fmaf(v[i][u].w, w, acc[i].w);
-                        lrun[i] = fmaf(sm_l[(u0 + u) * GP + hq[i]], w, lrun[i]);
+                        const float* mm = sm_m + (u0 + u) * GP + ha[i];
+                        const float* ll = sm_l + (u0 + u) * GP + ha[i];
+                        const float w0 = fast_exp2(mm[0] - mu[i][0]);
+                        const float w1 = fast_exp2(mm[1] - mu[i][1]);
+                        acc[i].x = fmaf(v[i][u].x, w0, acc[i].x);
+                        acc[i].y = fmaf(v[i][u].y, w1, acc[i].y);
+                        acc[i].z = fmaf(v[i][u].z, w0, acc[i].z);
+                        acc[i].w = fmaf(v[i][u].w, w1, acc[i].w);
+                        lrun[i][0] = fmaf(ll[0], w0, lrun[i][0]);
+                        lrun[i][1] = fmaf(ll[1], w1, lrun[i][1]);
                     }
                 }
         }
     }
 #pragma unroll
-    for (int i = 0; i < QPT; ++i) {
-        const int q = tid + i * NTHR;
-        if (q < nq) {
-            __half2* dst = reinterpret_cast<__half2*>(p.out + head_base * D + (size_t)q * 4);
-            dst[0] = __floats2half2_rn(lrun[i] > 0.f ? acc[i].x / lrun[i] : 0.f,
-                                       lrun[i] > 0.f ? acc[i].y / lrun[i] : 0.f);
-            dst[1] = __floats2half2_rn(lrun[i] > 0.f ? acc[i].z / lrun[i] : 0.f,
-                                       lrun[i] > 0.f ? acc[i].w / lrun[i] : 0.f);
+    for (int i = 0; i < FPT; ++i) {
+        const int f = tid + i * NTHR;
+        if (f >= NFRAG) continue;
+        const int d = (f / (32 * NT)) * 16 + ((f & 31) >> 2);
+        const float vals[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int h = ha[i] + (c & 1);
+            const float l = lrun[i][c & 1];
+            if (h < gcount)
+                p.out[(head_base + h) * D + d + ((c >> 1) << 3)] =
+                    __float2half_rn(l > 0.f ? vals[c] / l : 0.f);
         }
     }
 }
@@ -339,12 +395,16 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
     // costs - first tile, fold, piece store - weigh less, and the freed SM
     // slots let the next launch's CTAs start early).
     const long long T = seq_start[B];
+    CostMap cm{seq_start, B, upb, p.item_cost, p.merge_cost, 0, 0};
+    cm.Ctot = T + (long long)B * upb * (cm.xc + cm.mc);
     long long C = min((long long)gridDim.x, T);
     if (p.min_tiles_per_cta > 0)
         C = min(C, max((long long)p.min_ctas, T / p.min_tiles_per_cta));
+    C = max(1LL, min(C, cm.Ctot / (cm.xc + cm.mc + 2)));   // every CTA owns a tile
+    cm.C = C;
     if (blockIdx.x >= C) return;                    // uniform over the CTA
-    const int beg = int((blockIdx.x * T) / C);
-    const int end = int(((blockIdx.x + 1) * T) / C);
+    const int beg = cm.beg(blockIdx.x);
+    const int end = cm.beg(blockIdx.x + 1);
     const int n = end - beg;
     if (threadIdx.x == 0) FR_TRACE_EV(kEvMeta);
 
@@ -417,6 +477,10 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
     bool ok = true;
     TileCursor cur = start;
     int k = 0;
+    // the unit this CTA merges after its range (-1: none)
+    int m_unit = -1, m_cf = 0, m_cl = 0, m_gcount = 0;
+    bool m_cf_tail = false;
+    size_t m_head_base = 0;
     for (int e = 0; k < n; ++e) {
         const int b = cur.b, j = cur.j, nb = cur.nb, i0 = cur.i;
         const int cnt = min(nb - i0, n - k);
@@ -524,24 +588,24 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
             if (threadIdx.x == 0) FR_TRACE_EV(kEvStored);
             continue;
         }
-        // A piece of a unit shared with other CTAs: slot 2c (first item of
-        // this CTA) or 2c + 1 (its last); a timed-out CTA stores the neutral
-        // state (m = -inf, l = 0, acc = 0).
+        // A piece of a unit shared with other CTAs, in fragment order
+        // (merge_pieces), in slot 2c (first item of this CTA) or 2c + 1 (its
+        // last); a timed-out CTA stores the neutral state (m = -inf, l = 0,
+        // acc = 0).  The CTA holding the unit's last tile - whose range the
+        // cost map charged with the merge - merges it once its own range is
+        // done; it then waits (bounded) for the other pieces' counts.
         const int unit = b * upb + j;
         if (warp == 0) {
             const int slot = 2 * blockIdx.x + (e == 0 ? 0 : 1);
-            float* pa = p.part_acc + (size_t)slot * GP * D;
+            float4* pa = reinterpret_cast<float4*>(p.part_acc + (size_t)slot * GP * D);
             float* pm = p.part_ml + (size_t)slot * GP * 2;
 #pragma unroll
             for (int dm = 0; dm < DTILES; ++dm)
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const int d = dm * 16 + g + ((c >> 1) << 3);
-                        const int hj = nt * 8 + 2 * t + (c & 1);
-                        pa[hj * D + d] = ok_all ? o[dm][nt][c] : 0.f;
-                    }
+                    pa[(dm * NT + nt) * 32 + lane] =
+                        ok_all ? make_float4(o[dm][nt][0], o[dm][nt][1], o[dm][nt][2], o[dm][nt][3])
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
             if (g == 0) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
@@ -553,26 +617,40 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
                     }
             }
             __syncwarp();
-            if (lane == 0) {
-                const int cf = cta_of_tile(ustart, T, C);
-                const int cl = cta_of_tile(ustart + nb - 1, T, C);
-                // acq_rel: publishes this warp's piece (ordered before by
-                // __syncwarp) and, for the last arriver, acquires the others.
-                const int old = atom_add_acq_rel_gpu(&p.counters[unit], 1);
-                const bool last = old == cl - cf;
-                if (last) p.counters[unit] = 0;         // every piece has been counted
-                xflag[0] = last ? 1 : 0;
-                xflag[1] = cf;
-                xflag[2] = cl;
+            // release: publishes this warp's piece (ordered before it by __syncwarp)
+            if (lane == 0) red_add_release_gpu(&p.counters[unit], 1);
+        }
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvStored);
+        if (e == 0 && i0 + cnt == nb) {                // this CTA holds the unit's last tile
+            m_unit = unit;
+            m_cf = cm.cta_of(b, j, nb, 0);
+            m_cl = blockIdx.x;
+            m_cf_tail = cm.beg(m_cf) < ustart;
+            m_gcount = gcount;
+            m_head_base = head_base;
+        }
+    }
+
+    // ---- deferred merge of the unit whose last tile this CTA holds: wait
+    // (bounded) until every contributor's piece is counted, merge, re-arm.
+    if (m_unit >= 0) {
+        const int want = m_cl - m_cf + 1;
+        if (threadIdx.x == 0) {
+            if (ld_acquire_gpu(&p.counters[m_unit]) < want) {
+                const unsigned long long t0 = globaltimer_ns();
+                while (ld_acquire_gpu(&p.counters[m_unit]) < want) {
+                    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                        record_error(p.err, kDevTimeoutPeer);
+                        break;
+                    }
+                }
             }
         }
-        consumer_sync(NW * 32);
-        if (threadIdx.x == 0) FR_TRACE_EV(kEvStored);
-        if (xflag[0]) {
-            const int cf = xflag[1], cl = xflag[2];
-            const bool cf_tail = (int)((cf * T) / C) < ustart;   // the unit is cf's last item
-            merge_pieces<D, NT, NW>(p, xarea, cf, cl, cf_tail, gcount, head_base);
-            if (threadIdx.x == 0) FR_TRACE_EV(kEvMergeEnd);
+        consumer_sync(NW * 32);                        // the pieces are visible to every thread
+        merge_pieces<D, NT, NW>(p, xarea, m_cf, m_cl, m_cf_tail, m_gcount, m_head_base);
+        if (threadIdx.x == 0) {
+            p.counters[m_unit] = 0;                    // every piece was counted: re-arm
+            FR_TRACE_EV(kEvMergeEnd);
         }
     }
 }

@@ -573,6 +573,12 @@ int run_persistent(DecodeParams p, int head_dim, int batch, int max_kv_len, __ha
     static const int min_tiles = env_int("FORGERT_PERSIST_MIN_TILES", 16);
     p.min_tiles_per_cta = std::max(0, min_tiles);
     p.min_ctas = st->sm_count;
+    // Partition cost of starting an item and of merging a unit, in tile
+    // times (FORGERT_PERSIST_ITEM_COST / _MERGE_COST, read once).
+    static const int item_cost = std::max(0, env_int("FORGERT_PERSIST_ITEM_COST", 4));
+    static const int merge_cost = std::max(0, env_int("FORGERT_PERSIST_MERGE_COST", 4));
+    p.item_cost = item_cost;
+    p.merge_cost = merge_cost;
     static const int trace_plan = env_int("FORGERT_TRACE_PLAN", 0);
     if (trace_plan)
         std::fprintf(stderr, "[forgert] persistent D=%d batch=%d units=%d ctas=%d prefetch=%d\n",

@@ -84,6 +84,10 @@ struct DecodeParams {
     // min_tiles_per_cta tiles, never fewer than min_ctas (0 = all of them).
     int min_tiles_per_cta;
     int min_ctas;
+    // Cost map of the persistent partition (tile-times): per unit, item_cost
+    // before its first tile and merge_cost after its last.
+    int item_cost;
+    int merge_cost;
     // Paged KV (kernel instantiated with PAGED): the tensor maps view the page
     // pool [num_pages * page_size rows][Hkv][D/64][64]; logical position t of
     // sequence b is row block_table[b * bt_stride + t / page_size] * page_size

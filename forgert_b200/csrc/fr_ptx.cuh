@@ -196,6 +196,18 @@ __device__ __forceinline__ void st_dsmem_u32(uint32_t addr, uint32_t v) {
 // Atomic add with acquire-release semantics at GPU scope: orders every write
 // this thread has observed (including other threads' writes published to it
 // by a barrier) before the add, and the add before later reads.
+// Release increment (no value returned): publishes the stores this thread
+// has observed (e.g. its warp's, ordered before by __syncwarp).
+__device__ __forceinline__ void red_add_release_gpu(int* addr, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" :: "l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* addr) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
     int old;
     asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;"

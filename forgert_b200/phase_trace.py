@@ -49,6 +49,7 @@ def parse(argv=None):
     ap.add_argument("--replays", type=int, default=4)
     ap.add_argument("--no-overlap", action="store_true")
     ap.add_argument("--gemm", action="store_true")
+    ap.add_argument("--dump", default=None, help="also save the raw records (.npz, one array per CTA)")
     return ap.parse_args(argv)
 
 
@@ -187,6 +188,8 @@ def main(argv=None):
     per_cta = {c: allrec[c, :min(int(fill[c]), PER_CTA)] for c in range(MAX_CTAS) if fill[c]}
     n = int(sum(min(int(f), PER_CTA) for f in fill))
     res = summarise(per_cta)
+    if args.dump:
+        np.savez_compressed(args.dump, **{f"cta{c}": r for c, r in per_cta.items()})
     res["workload"] = {"name": args.workload, "kv_len": args.kv if args.workload == "cfg2" else None,
                        "shard": args.shard if args.workload == "cfg3" else None,
                        "layers": args.layers, "replays": args.replays,
