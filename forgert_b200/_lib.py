@@ -36,6 +36,7 @@ SIGNATURES = {
     "fr_lse_merge_strided": (_i, [_vp, _vp, _i, _vp, _i, _i, ctypes.c_longlong,
                                   ctypes.c_longlong, _vp]),
     "fr_rope_tables": (_i, [_vp, _vp, _i, _i, ctypes.c_float, ctypes.c_float]),
+    "fr_rope_tables_device": (_i, [_vp, _vp, _i, _i, ctypes.c_float, ctypes.c_float, _vp]),
     "fr_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "fr_qkv_bias_rope_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i,
                                      _i, _i, _i, _vp]),

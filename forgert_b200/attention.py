@@ -19,6 +19,7 @@ __all__ = [
     "ForgeRTError", "decode_attn_v4_flash", "decode_attn_v0_naive", "decode_attn_v1_coal",
     "decode_attn_v2_warp_red", "decode_attn_v3_vec", "prefill_attn_causal",
     "decode_attn_batched", "decode_attn_partial", "lse_merge", "rope_precompute_tables",
+    "rope_tables_device",
     "rope_append", "reserve_workspace", "decode_workspace_size", "device_error",
 ]
 
@@ -132,6 +133,23 @@ def rope_precompute_tables(max_seq_len: int, head_dim: int, base: float, scale: 
     with torch.cuda.device(dev):
         check("fr_rope_tables", lib.fr_rope_tables(
             cos.data_ptr(), sin.data_ptr(), max_seq_len, head_dim, float(base), float(scale)))
+    return cos, sin
+
+
+def rope_tables_device(max_seq_len: int, head_dim: int, base: float, scale: float = 1.0,
+                       device=None, stream=None):
+    """The reference's own table values (fast single-precision arithmetic,
+    kernels/rope.cu:28-42), computed on the device; returns (cos, sin)."""
+    import torch
+
+    lib = load()
+    dev = torch.device("cuda") if device is None else torch.device(device)
+    cos = torch.empty((max_seq_len, head_dim // 2), dtype=torch.float32, device=dev)
+    sin = torch.empty_like(cos)
+    with torch.cuda.device(dev):
+        check("fr_rope_tables_device", lib.fr_rope_tables_device(
+            cos.data_ptr(), sin.data_ptr(), max_seq_len, head_dim, float(base), float(scale),
+            _stream(stream)))
     return cos, sin
 
 

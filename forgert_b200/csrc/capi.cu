@@ -1139,6 +1139,22 @@ int fr_rope_tables(float* cos_tab, float* sin_tab, int max_seq_len, int head_dim
     return FR_OK;
 }
 
+int fr_rope_tables_device(float* cos_tab, float* sin_tab, int max_seq_len, int head_dim,
+                          float base, float scale, void* stream) {
+    if (!cos_tab || !sin_tab || max_seq_len <= 0 || head_dim <= 0 || (head_dim & 1) ||
+        !(base > 0.f) || !(scale > 0.f))
+        return FR_ERR_INVALID_ARG;
+    const long long n = (long long)max_seq_len * (head_dim / 2);
+    if (n >= (1LL << 31)) return FR_ERR_INVALID_ARG;
+    const int threads = 256;
+    fr::rope_tables_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0,
+                             static_cast<cudaStream_t>(stream)>>>(cos_tab, sin_tab, max_seq_len,
+                                                                  head_dim, base, scale);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FR_OK : cuda_fail(e);
+}
+
 int fr_qkv_bias_rope_append(void* q, void* k, void* v, const void* q_bias, const void* k_bias,
                             const void* v_bias, void* k_cache, void* v_cache,
                             const float* cos_tab, const float* sin_tab, int seq_len,

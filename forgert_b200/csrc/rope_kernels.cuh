@@ -91,4 +91,25 @@ rope_append_kernel(__half* __restrict__ q, __half* __restrict__ k, __half* __res
     vdst[vi] = xv;
 }
 
+// RoPE tables on the device with the reference's single-precision
+// arithmetic.  The reference builds them with
+//   theta = pos / (powf(base, 2 * f / head_dim) * scale), cosf, sinf
+// (kernels/rope.cu:28-42) compiled with --use_fast_math, which turns the
+// two divisions, powf, cosf and sinf into the fast approximate intrinsics;
+// calling those intrinsics here gives the same table values (the fast
+// sine/cosine lose accuracy as theta grows, which the tables then share).
+// One thread per (pos, f); grid covers max_seq_len * head_dim / 2 entries.
+__global__ void rope_tables_kernel(float* __restrict__ cos_tab, float* __restrict__ sin_tab,
+                                   int max_seq_len, int head_dim, float base, float scale) {
+    const int half_d = head_dim >> 1;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)max_seq_len * half_d) return;
+    const int pos = (int)(i / half_d);
+    const int f = (int)(i - (long long)pos * half_d);
+    const float expo = __fdividef(2.0f * (float)f, (float)head_dim);
+    const float theta = __fdividef((float)pos, __powf(base, expo) * scale);
+    cos_tab[i] = __cosf(theta);
+    sin_tab[i] = __sinf(theta);
+}
+
 }  // namespace fr

@@ -200,6 +200,17 @@ FR_API int fr_exchange_wait_limit_ms(void);
 FR_API int fr_rope_tables(float* cos_tab, float* sin_tab, int max_seq_len, int head_dim, float base,
                    float scale);
 
+/* RoPE cos/sin tables [max_seq_len, head_dim/2] fp32 computed on the device,
+ * stream-ordered, with the reference's own single-precision arithmetic: the
+ * same values as rope_precompute_tables (kernels/rope.cu:28-56, built with
+ * --use_fast_math, whose fast sine and cosine drift from the exact values as
+ * theta = pos / base^(2f/D) grows - up to ~16000 rad at max_seq_len 16384).
+ * Use it where results must match the reference engine bit for bit;
+ * fr_rope_tables gives the exactly rounded tables.  Caller-allocated
+ * buffers; replaces rope_precompute_tables minus its allocation. */
+FR_API int fr_rope_tables_device(float* cos_tab, float* sin_tab, int max_seq_len, int head_dim,
+                                 float base, float scale, void* stream);
+
 /* Fused decode prologue: NeoX (half-split) RoPE on q and k in place for
  * tokens t < seq_len at position pos_offset + t, then appends the rotated k
  * and v rows to the layer cache at row pos_offset + t.  Replaces the

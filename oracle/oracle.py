@@ -88,6 +88,9 @@ def load_ref() -> ctypes.CDLL | None:
         lib.ref_prefill_attn_causal.argtypes = [vp, vp, vp, vp] + [ctypes.c_int] * 4 + [vp]
         lib.ref_rope_v2_fused.argtypes = [vp, vp, vp, vp] + [ctypes.c_int] * 5 + [vp]
         lib.ref_bias_add_broadcast.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int, vp]
+        lib.ref_rope_precompute_tables.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int,
+                                                   ctypes.c_float, ctypes.c_float]
+        lib.ref_rope_precompute_tables.restype = ctypes.c_int
         lib.ref_run_kernel_tests.restype = ctypes.c_int
         _ref_lib = lib
     return _ref_lib

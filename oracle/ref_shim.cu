@@ -71,6 +71,21 @@ void ref_rope_v2_fused(void* q, void* k, const float* cos_tab, const float* sin_
                   num_q_heads, num_kv_heads, head_dim, pos_offset, static_cast<cudaStream_t>(stream));
 }
 
+// The reference's RoPE tables (kernels/rope.cu:28-56: its own allocation and
+// kernel), copied into caller-owned device buffers.
+int ref_rope_precompute_tables(float* cos_out, float* sin_out, int max_seq_len, int head_dim,
+                               float base, float scale) {
+    float* c = nullptr;
+    float* s = nullptr;
+    rope_precompute_tables(&c, &s, max_seq_len, head_dim, base, scale);
+    const size_t bytes = (size_t)max_seq_len * (head_dim / 2) * sizeof(float);
+    cudaError_t e = cudaMemcpy(cos_out, c, bytes, cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(sin_out, s, bytes, cudaMemcpyDeviceToDevice);
+    cudaFree(c);
+    cudaFree(s);
+    return (int)e;
+}
+
 void ref_bias_add_broadcast(void* out, const void* bias, int seq_len, int hidden, void* stream) {
     bias_add_broadcast(static_cast<__half*>(out), static_cast<const __half*>(bias), seq_len,
                        hidden, static_cast<cudaStream_t>(stream));
