@@ -25,6 +25,16 @@
 #include "forgert_attn.h"
 
 namespace forgert_b200_detail {
+// The default stream of the including translation unit: a null stream means
+// the legacy default stream, or this thread's default stream when the
+// caller is compiled with --default-stream per-thread (as a launch
+// `<<<g, b, 0, nullptr>>>` in that unit would).
+inline void* caller_stream(cudaStream_t stream) {
+#ifdef CUDA_API_PER_THREAD_DEFAULT_STREAM
+    if (stream == nullptr) return static_cast<void*>(cudaStreamPerThread);
+#endif
+    return static_cast<void*>(stream);
+}
 inline void throw_if(int status, const char* fn) {
     if (status != FR_OK)
         throw std::runtime_error(std::string("forgert_b200 ") + fn + ": " +
@@ -34,7 +44,7 @@ inline void decode(const __half* q, const __half* k_cache, const __half* v_cache
                    int num_heads, int num_kv_heads, int head_dim, int kv_len,
                    cudaStream_t stream, const char* fn) {
     throw_if(fr_decode_attn(q, k_cache, v_cache, out, num_heads, num_kv_heads, head_dim, kv_len,
-                            static_cast<void*>(stream)),
+                            caller_stream(stream)),
              fn);
 }
 }  // namespace forgert_b200_detail
@@ -91,6 +101,6 @@ inline void prefill_attn_causal(const __half* __restrict__ q, const __half* __re
                                 cudaStream_t stream = nullptr) {
     forgert_b200_detail::throw_if(
         fr_prefill_attn(q, k, v, out, seq_len, num_heads, num_kv_heads, head_dim,
-                        static_cast<void*>(stream)),
+                        forgert_b200_detail::caller_stream(stream)),
         "prefill_attn_causal");
 }
