@@ -194,44 +194,6 @@ struct CostMap {
     }
 };
 
-// Cross-warp fold, one 8-head tile (nt) at a time: this lane's O^T
-// fragments and its columns' (m, l) into / out of a row of the exchange area.
-template <int D, int NT>
-__device__ __forceinline__ void x_store(float* row, const float (&o)[D / 16][NT][4],
-                                        const float (&m)[NT][2], const float (&l)[NT][2], int nt) {
-#pragma unroll
-    for (int dm = 0; dm < D / 16; ++dm)
-        *reinterpret_cast<float4*>(row + dm * 4) =
-            make_float4(o[dm][nt][0], o[dm][nt][1], o[dm][nt][2], o[dm][nt][3]);
-    *reinterpret_cast<float4*>(row + (D / 16) * 4) =
-        make_float4(m[nt][0], m[nt][1], l[nt][0], l[nt][1]);
-}
-
-template <int D, int NT>
-__device__ __forceinline__ void x_fold(const float* row, float (&o)[D / 16][NT][4],
-                                       float (&m)[NT][2], float (&l)[NT][2], int nt) {
-    const float4 ml = *reinterpret_cast<const float4*>(row + (D / 16) * 4);
-    const float mo[2] = {ml.x, ml.y}, lo[2] = {ml.z, ml.w};
-    float sa[2], sb[2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const float mn = fmaxf(m[nt][j], mo[j]);
-        const float mu = (mn == -INFINITY) ? 0.f : mn;
-        sa[j] = fast_exp2(m[nt][j] - mu);
-        sb[j] = fast_exp2(mo[j] - mu);
-        l[nt][j] = fmaf(l[nt][j], sa[j], lo[j] * sb[j]);
-        m[nt][j] = mn;
-    }
-#pragma unroll
-    for (int dm = 0; dm < D / 16; ++dm) {
-        const float4 v = *reinterpret_cast<const float4*>(row + dm * 4);
-        o[dm][nt][0] = fmaf(o[dm][nt][0], sa[0], v.x * sb[0]);
-        o[dm][nt][1] = fmaf(o[dm][nt][1], sa[1], v.y * sb[1]);
-        o[dm][nt][2] = fmaf(o[dm][nt][2], sa[0], v.z * sb[0]);
-        o[dm][nt][3] = fmaf(o[dm][nt][3], sa[1], v.w * sb[1]);
-    }
-}
-
 // Merges the pieces of a unit, stored by contributors cf..cl (CTA c's slot is
 // 2c, or 2c + 1 for cf when the unit is not its first item), into the fp16
 // output of the unit's gcount heads.  Pieces are kept in the consumer
@@ -466,7 +428,16 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
     }
 
     // ------------------------------------------------------------ consumers
-    if (p.prefetch_meta) grid_dependency_wait();   // q and the outputs depend on it
+    if (p.prefetch_meta) {
+        // q and the outputs depend on the preceding grid; only an L2 prefetch
+        // of the first item's q lines may go before the wait (L2 stays
+        // coherent, so a line the preceding kernel then writes is updated)
+        const int kvh0 = start.j / hg, hg0 = start.j - kvh0 * hg;
+        const int gc0 = min(GP, p.G - hg0 * GP);
+        if (warp == 0 && lane < (gc0 * D * 2 + 127) / 128)
+            prefetch_l2(p.q + ((size_t)start.b * p.H + kvh0 * p.G + hg0 * GP) * D + lane * 64);
+        grid_dependency_wait();
+    }
     if (threadIdx.x == 0) FR_TRACE_EV(kEvDepWait);
     const int g = lane >> 2;
     const int t = lane & 3;

@@ -213,6 +213,44 @@ __device__ __forceinline__ uint32_t swz_offset(int r, int col) {
     return uint32_t(sub * TILE * 128 + r * 128 + ((chunk ^ (r & 7)) << 4));
 }
 
+// Cross-warp fold, one 8-head tile (nt) at a time: this lane's O^T
+// fragments and its columns' (m, l) into / out of a row of the exchange area.
+template <int D, int NT>
+__device__ __forceinline__ void x_store(float* row, const float (&o)[D / 16][NT][4],
+                                        const float (&m)[NT][2], const float (&l)[NT][2], int nt) {
+#pragma unroll
+    for (int dm = 0; dm < D / 16; ++dm)
+        *reinterpret_cast<float4*>(row + dm * 4) =
+            make_float4(o[dm][nt][0], o[dm][nt][1], o[dm][nt][2], o[dm][nt][3]);
+    *reinterpret_cast<float4*>(row + (D / 16) * 4) =
+        make_float4(m[nt][0], m[nt][1], l[nt][0], l[nt][1]);
+}
+
+template <int D, int NT>
+__device__ __forceinline__ void x_fold(const float* row, float (&o)[D / 16][NT][4],
+                                       float (&m)[NT][2], float (&l)[NT][2], int nt) {
+    const float4 ml = *reinterpret_cast<const float4*>(row + (D / 16) * 4);
+    const float mo[2] = {ml.x, ml.y}, lo[2] = {ml.z, ml.w};
+    float sa[2], sb[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const float mn = fmaxf(m[nt][j], mo[j]);
+        const float mu = (mn == -INFINITY) ? 0.f : mn;
+        sa[j] = fast_exp2(m[nt][j] - mu);
+        sb[j] = fast_exp2(mo[j] - mu);
+        l[nt][j] = fmaf(l[nt][j], sa[j], lo[j] * sb[j]);
+        m[nt][j] = mn;
+    }
+#pragma unroll
+    for (int dm = 0; dm < D / 16; ++dm) {
+        const float4 v = *reinterpret_cast<const float4*>(row + dm * 4);
+        o[dm][nt][0] = fmaf(o[dm][nt][0], sa[0], v.x * sb[0]);
+        o[dm][nt][1] = fmaf(o[dm][nt][1], sa[1], v.y * sb[1]);
+        o[dm][nt][2] = fmaf(o[dm][nt][2], sa[0], v.z * sb[0]);
+        o[dm][nt][3] = fmaf(o[dm][nt][3], sa[1], v.w * sb[1]);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // One consumer warp's share of one K/V tile: rows row0 .. row0 + 15 of the
 // stage at kst / vst (shared-memory addresses; vgen = the V stage's generic
@@ -551,7 +589,11 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         __syncwarp();
     } else {
         // -------------------------------------------------------- consumers
-        // q (and everything this CTA writes) depends on the preceding grid.
+        // q (and everything this CTA writes) depends on the preceding grid:
+        // only an L2 prefetch of its lines may go before the wait (L2 stays
+        // coherent, so a line the preceding kernel then writes is updated).
+        if (warp == 0 && lane < (gcount * D * 2 + 127) / 128)
+            prefetch_l2(p.q + ((size_t)b * p.H + h0) * D + lane * 64);
         grid_dependency_wait();
         if (threadIdx.x == 0) FR_TRACE_EV(kEvDepWait);
 

@@ -102,6 +102,11 @@ __device__ __forceinline__ void tma_load_4d(void* dst_smem, const void* tmap, in
         : "memory");
 }
 
+// Prefetch of one global line into L2 (a hint; nothing is returned).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" :: "l"(p) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
 }
