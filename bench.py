@@ -803,8 +803,12 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     roofline = {
         "bound": "hbm", "kernel": kern, "achieved": round(achieved, 1), "peak": peak,
         "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-        "traffic": (tr.get("dram_bytes_per_launch") if tr else None),
-        "traffic_scope": (tr.get("scope") if tr else None),
+        # DRAM bytes of one full-size capture, scaled to this GPU's call by
+        # the algorithmic bytes it processes (traffic grows with them)
+        "traffic": (int(tr["dram_bytes_per_launch"] * head_call_bytes /
+                        tr["algorithmic_bytes_per_launch"]) if tr else None),
+        "traffic_scope": (f"{tr.get('scope')}, scaled to this call's algorithmic bytes"
+                          if tr else None),
         "algorithmic_bytes_per_launch": head_call_bytes,
         "how": "achieved = algorithmic bytes of one call on this GPU / (device time of the "
                "timed steps / calls per step); rank 0's calls",
