@@ -794,7 +794,7 @@ def run_ours(args, torch, dist, rank, local_rank, world):
     tr = traffic_record(f"{args.workload}_call") if args.workload in ("cfg3", "cfg4") else \
         traffic_record("cfg2_kv16384") if args.workload == "cfg2" else None
     achieved = head_call_bytes / (stats[str(dom_key)]["us_per_call"] * 1e-6) / 1e9
-    kern = {"cfg3": "split_decode_kernel, batched (fr_decode_attn_batched): one call per layer",
+    kern = {"cfg3": "persistent_decode_kernel (fr_decode_attn_batched): one call per layer",
             "cfg3p": "split_decode_kernel, paged (fr_decode_attn_paged)",
             "cfg4": "split_decode_kernel (fr_decode_attn / fr_decode_attn_exchange), one call "
                     "per layer",
@@ -832,8 +832,12 @@ def run_ours(args, torch, dist, rank, local_rank, world):
         line["sub"] = sub
     if world == 1 and not shard and not args.no_cpu_baseline and not args.ncu and \
             args.workload == "cfg3":
-        line["cpu_baseline"] = cpu_baseline_cfg3(budget_s=12.0)
-        line["cpu_baseline_hf"] = cpu_baseline_hf_cfg3(budget_s=8.0)
+        # in a fresh process, as the reference arm runs: none of this
+        # process's threads, pinned buffers or allocator state competes
+        import multiprocessing as mp
+        with mp.get_context("spawn").Pool(1) as pool:
+            line["cpu_baseline"] = pool.apply(cpu_baseline_cfg3, (12.0,))
+            line["cpu_baseline_hf"] = pool.apply(cpu_baseline_hf_cfg3, (8.0,))
     emit(line)
 
 
