@@ -24,13 +24,13 @@
 // through a small shared-memory exchange area in two rounds (warps 2,3 ->
 // 0,1 -> 0).  Warp 0 then writes the normalised fp16 output (whole unit) or
 // stores the piece's (m, l, acc) state in the CTA's partial slot (2c for
-// its first item, 2c + 1 for its last) and counts it on the unit's counter.
-// The CTA holding a unit's last tile merges the unit after its own range
-// (bounded wait until every piece is counted, log-sum-exp merge, re-arm);
-// all CTAs of the grid are resident by then, since the next grid can launch
-// only once every CTA of this one has started.  Meanwhile the producer warp
-// keeps streaming the next item's tiles through the TMA ring: the ring never
-// drains at item boundaries.
+// its first item, 2c + 1 for its last); the pieces are counted on their
+// units' counters after the range (one fence, then an atomic per piece).
+// The contributor whose count completes a unit merges it after its own range
+// (log-sum-exp merge of the pieces in contributor order - the result does
+// not depend on who merges - and re-arm): no CTA ever waits for another.
+// Meanwhile the producer warp keeps streaming the next item's tiles through
+// the TMA ring: the ring never drains at item boundaries.
 //
 // Metadata: every CTA reads kv_lens (B <= kPersistMaxBatch) and forms the
 // tile prefix in shared memory with a block-wide scan; row_offsets are read
@@ -153,8 +153,8 @@ struct TileCursor {
 
 // Cost-balanced partition.  Every unit costs its tiles plus `xc` tile-times
 // placed before its first tile (starting an item: q load, and the fold and
-// piece store of the item it ends) and `mc` after its last tile (its merge,
-// done by the CTA holding that tile).  In cost space unit j of sequence b
+// piece store of the item it ends) and `mc` after its last tile (a share of
+// the merge cost, charged to the CTA holding that tile).  In cost space unit j of sequence b
 // spans xc + nb + mc points from cs(b) + j * (nb + xc + mc), the sequence's
 // cost start being cs(b) = seq_start[b] + (xc + mc) * upb * b.  CTA c owns
 // the cost range [c*Ctot/C, (c+1)*Ctot/C);
@@ -200,87 +200,102 @@ struct CostMap {
 // fragment order - slot [dm][nt][lane] float4 = o[dm][nt][0..3] of that
 // lane, then (m, l) per head - so every thread folds whole float4
 // fragments: fragment f = (dm, nt, lane) holds heads nt*8 + 2(lane&3) +
-// {0,1} at dims dm*16 + lane/4 + {0,8}.  Contributors go in chunks: their
-// (m, l) pairs are staged in shared memory with one round of loads, then
-// each thread folds its fragments with UB contributors' loads in flight.
-// All consumer threads take part.
+// {0,1} at dims dm*16 + lane/4 + {0,8}.
+//
+// Contributors go in chunks of KW = threads / GP.  Per chunk the first UB
+// contributors' fragments are requested first; meanwhile thread (head h,
+// contributor u) loads that piece's (m, l), the KW lanes of a head form the
+// chunk's maximum and weighted row sum by shuffles, and the weights
+// 2^(m_u - m) go to shared memory; after one barrier every thread folds its
+// fragments with FMAs only.  The order of the sums is fixed (contributor
+// order within a lane group, lanes by shuffle tree), so the result does not
+// depend on which CTA merges.  All consumer threads take part.
 template <int D, int NT, int NW>
 __device__ __forceinline__ void merge_pieces(const DecodeParams& p, float* area, int cf, int cl,
                                              bool cf_tail, int gcount, size_t head_base) {
     constexpr int GP = NT * 8;
     constexpr int DTILES = D / 16;
     constexpr int NTHR = NW * 32;
-    constexpr int XFL = 2 * 32 * ((D / 16) * 4 + 4);      // floats of the exchange area
-    constexpr int KC = XFL / (2 * GP);                    // contributors per chunk
+    constexpr int KW = NTHR / GP;                         // contributors per chunk
     constexpr int NFRAG = DTILES * NT * 32;               // float4 fragments per piece
-    constexpr int FPT = (NFRAG + NTHR - 1) / NTHR;        // fragments per thread
-    constexpr int UB = FPT <= 2 ? 8 : 2;                  // contributors per load batch
-    float* sm_m = area;                                   // [KC][GP]
-    float* sm_l = area + KC * GP;                         // [KC][GP]
+    constexpr int FPT = NFRAG / NTHR;                     // fragments per thread
+    constexpr int UB = 16 / FPT;                          // contributors per load batch
+    static_assert(NFRAG % NTHR == 0 && KW <= 32 && 32 % KW == 0, "merge thread layout");
+    float* sm_w = area;                                   // [KW][GP] chunk weights
+    float* sm_r = sm_w + KW * GP;                         // [GP] rescale of the running state
+    float* sm_inv = sm_r + GP;                            // [GP] 1 / final row sum
     const int tid = threadIdx.x;
+    const int wh = tid / KW, wu = tid - (tid / KW) * KW;  // weight thread: head, contributor
+    float mrun = -INFINITY, lrun = 0.f;                   // head wh's running state (its KW lanes)
     float4 acc[FPT];
-    float mrun[FPT][2], lrun[FPT][2];
     int ha[FPT];                                          // first head of the fragment
 #pragma unroll
     for (int i = 0; i < FPT; ++i) {
         acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        mrun[i][0] = mrun[i][1] = -INFINITY;
-        lrun[i][0] = lrun[i][1] = 0.f;
         const int f = tid + i * NTHR;
         ha[i] = ((f >> 5) % NT) * 8 + 2 * (f & 3);
     }
     auto slot_of = [&](int cc) { return 2 * cc + ((cc == cf && cf_tail) ? 1 : 0); };
     const int k_all = cl - cf + 1;
-    for (int c0 = 0; c0 < k_all; c0 += KC) {
-        const int kc = min(KC, k_all - c0);
-        consumer_sync(NTHR);                              // the previous chunk is folded
-        for (int idx = tid; idx < kc * GP; idx += NTHR) {
-            const int u = idx / GP, h = idx - (idx / GP) * GP;
-            const float* pm = p.part_ml + ((size_t)slot_of(cf + c0 + u) * GP + h) * 2;
-            sm_m[idx] = __ldcg(pm);
-            sm_l[idx] = __ldcg(pm + 1);
-        }
-        consumer_sync(NTHR);
-        float mu[FPT][2];
-#pragma unroll
-        for (int i = 0; i < FPT; ++i)
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                float cm = mrun[i][j];
-                for (int u = 0; u < kc; ++u) cm = fmaxf(cm, sm_m[u * GP + ha[i] + j]);
-                mu[i][j] = (cm == -INFINITY) ? 0.f : cm;
-                const float r = fast_exp2(mrun[i][j] - mu[i][j]);
-                lrun[i][j] *= r;
-                if (j == 0) { acc[i].x *= r; acc[i].z *= r; } else { acc[i].y *= r; acc[i].w *= r; }
-                mrun[i][j] = cm;
-            }
-        for (int u0 = 0; u0 < kc; u0 += UB) {
-            float4 v[FPT][UB];
+    for (int c0 = 0; c0 < k_all; c0 += KW) {
+        const int kc = min(KW, k_all - c0);
+        float4 v[FPT][UB];
+        auto load_batch = [&](int u0) {
 #pragma unroll
             for (int i = 0; i < FPT; ++i)
 #pragma unroll
                 for (int u = 0; u < UB; ++u) {
                     const int f = tid + i * NTHR;
-                    const bool in = f < NFRAG && u0 + u < kc;
                     const float4* src = reinterpret_cast<const float4*>(
                         p.part_acc + (size_t)slot_of(cf + c0 + u0 + u) * GP * D) + f;
-                    v[i][u] = in ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    v[i][u] = u0 + u < kc ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
+        };
+        consumer_sync(NTHR);                              // the previous chunk's weights are used
+        load_batch(0);                                    // in flight with the (m, l) loads
+        float m = -INFINITY, l = 0.f;
+        if (wu < kc) {
+            const float* pm = p.part_ml + ((size_t)slot_of(cf + c0 + wu) * GP + wh) * 2;
+            m = __ldcg(pm);
+            l = __ldcg(pm + 1);
+        }
+        float mx = m;
+#pragma unroll
+        for (int o = 1; o < KW; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float mnew = fmaxf(mrun, mx);
+        const float muse = (mnew == -INFINITY) ? 0.f : mnew;
+        const float w = fast_exp2(m - muse);              // 0 for an empty piece (m = -inf)
+        const float r = fast_exp2(mrun - muse);
+        float ls = l * w;
+#pragma unroll
+        for (int o = 1; o < KW; o <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+        lrun = fmaf(lrun, r, ls);
+        mrun = mnew;
+        sm_w[wu * GP + wh] = w;
+        if (wu == 0) {
+            sm_r[wh] = r;
+            sm_inv[wh] = lrun > 0.f ? 1.f / lrun : 0.f;
+        }
+        consumer_sync(NTHR);
+        if (tid == 0) FR_TRACE_EV(kEvMergeLoaded);
+#pragma unroll
+        for (int i = 0; i < FPT; ++i) {
+            const float r0 = sm_r[ha[i]], r1 = sm_r[ha[i] + 1];
+            acc[i].x *= r0; acc[i].y *= r1; acc[i].z *= r0; acc[i].w *= r1;
+        }
+        for (int u0 = 0; u0 < kc; u0 += UB) {
+            if (u0 > 0) load_batch(u0);
 #pragma unroll
             for (int i = 0; i < FPT; ++i)
 #pragma unroll
                 for (int u = 0; u < UB; ++u) {
                     if (u0 + u < kc) {
-                        const float* mm = sm_m + (u0 + u) * GP + ha[i];
-                        const float* ll = sm_l + (u0 + u) * GP + ha[i];
-                        const float w0 = fast_exp2(mm[0] - mu[i][0]);
-                        const float w1 = fast_exp2(mm[1] - mu[i][1]);
+                        const float w0 = sm_w[(u0 + u) * GP + ha[i]];
+                        const float w1 = sm_w[(u0 + u) * GP + ha[i] + 1];
                         acc[i].x = fmaf(v[i][u].x, w0, acc[i].x);
                         acc[i].y = fmaf(v[i][u].y, w1, acc[i].y);
                         acc[i].z = fmaf(v[i][u].z, w0, acc[i].z);
                         acc[i].w = fmaf(v[i][u].w, w1, acc[i].w);
-                        lrun[i][0] = fmaf(ll[0], w0, lrun[i][0]);
-                        lrun[i][1] = fmaf(ll[1], w1, lrun[i][1]);
                     }
                 }
         }
@@ -288,16 +303,13 @@ __device__ __forceinline__ void merge_pieces(const DecodeParams& p, float* area,
 #pragma unroll
     for (int i = 0; i < FPT; ++i) {
         const int f = tid + i * NTHR;
-        if (f >= NFRAG) continue;
         const int d = (f / (32 * NT)) * 16 + ((f & 31) >> 2);
         const float vals[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const int h = ha[i] + (c & 1);
-            const float l = lrun[i][c & 1];
             if (h < gcount)
-                p.out[(head_base + h) * D + d + ((c >> 1) << 3)] =
-                    __float2half_rn(l > 0.f ? vals[c] / l : 0.f);
+                p.out[(head_base + h) * D + d + ((c >> 1) << 3)] = __float2half_rn(vals[c] * sm_inv[h]);
         }
     }
 }
@@ -428,6 +440,30 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
     }
 
     // ------------------------------------------------------------ consumers
+    // Merge bookkeeping of the range's first and last item, worked out while
+    // the preceding grid still runs (with launch overlap): xm[6r..6r+5] =
+    // unit (-1: not shared with other CTAs), first and last contributor,
+    // whether the unit is not the first contributor's first item, sequence,
+    // unit index; r = 0 for the first item (slot 2c), 1 for the last (2c + 1).
+    int* xm = xflag + 2;
+    if (threadIdx.x == 0) {
+        TileCursor lc;
+        lc.seek(seq_start, B, upb, end - 1);
+        const bool one = start.b == lc.b && start.j == lc.j;
+        auto note = [&](int r, int bb, int jj, int nbb, bool shared) {
+            int* m = xm + 6 * r;
+            m[0] = shared ? bb * upb + jj : -1;
+            if (!shared) return;
+            m[1] = cm.cta_of(bb, jj, nbb, 0);
+            m[2] = cm.cta_of(bb, jj, nbb, nbb - 1);
+            m[3] = cm.beg(m[1]) < seq_start[bb] + jj * nbb ? 1 : 0;
+            m[4] = bb;
+            m[5] = jj;
+        };
+        note(0, start.b, start.j, start.nb,
+             one ? !(start.i == 0 && lc.i == lc.nb - 1) : start.i != 0);
+        note(1, lc.b, lc.j, lc.nb, !one && lc.i != lc.nb - 1);
+    }
     if (p.prefetch_meta) {
         // q and the outputs depend on the preceding grid; only an L2 prefetch
         // of the first item's q lines may go before the wait (L2 stays
@@ -448,10 +484,6 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
     bool ok = true;
     TileCursor cur = start;
     int k = 0;
-    // the unit this CTA merges after its range (-1: none)
-    int m_unit = -1, m_cf = 0, m_cl = 0, m_gcount = 0;
-    bool m_cf_tail = false;
-    size_t m_head_base = 0;
     for (int e = 0; k < n; ++e) {
         const int b = cur.b, j = cur.j, nb = cur.nb, i0 = cur.i;
         const int cnt = min(nb - i0, n - k);
@@ -562,10 +594,10 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
         // A piece of a unit shared with other CTAs, in fragment order
         // (merge_pieces), in slot 2c (first item of this CTA) or 2c + 1 (its
         // last); a timed-out CTA stores the neutral state (m = -inf, l = 0,
-        // acc = 0).  The CTA holding the unit's last tile - whose range the
-        // cost map charged with the merge - merges it once its own range is
-        // done; it then waits (bounded) for the other pieces' counts.
-        const int unit = b * upb + j;
+        // acc = 0).  The stores are not waited for here: under the full
+        // K/V stream a fence takes microseconds, and a first item's fence
+        // would stall the ring for the items behind it.  Pieces are counted
+        // after the range.
         if (warp == 0) {
             const int slot = 2 * blockIdx.x + (e == 0 ? 0 : 1);
             float4* pa = reinterpret_cast<float4*>(p.part_acc + (size_t)slot * GP * D);
@@ -587,40 +619,45 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
                         pm[hj * 2 + 1] = ok_all ? l_run[nt][jj] : 0.f;
                     }
             }
-            __syncwarp();
-            // release: publishes this warp's piece (ordered before it by __syncwarp)
-            if (lane == 0) red_add_release_gpu(&p.counters[unit], 1);
         }
         if (threadIdx.x == 0) FR_TRACE_EV(kEvStored);
-        if (e == 0 && i0 + cnt == nb) {                // this CTA holds the unit's last tile
-            m_unit = unit;
-            m_cf = cm.cta_of(b, j, nb, 0);
-            m_cl = blockIdx.x;
-            m_cf_tail = cm.beg(m_cf) < ustart;
-            m_gcount = gcount;
-            m_head_base = head_base;
-        }
     }
 
-    // ---- deferred merge of the unit whose last tile this CTA holds: wait
-    // (bounded) until every contributor's piece is counted, merge, re-arm.
-    if (m_unit >= 0) {
-        const int want = m_cl - m_cf + 1;
-        if (threadIdx.x == 0) {
-            if (ld_acquire_gpu(&p.counters[m_unit]) < want) {
-                const unsigned long long t0 = globaltimer_ns();
-                while (ld_acquire_gpu(&p.counters[m_unit]) < want) {
-                    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                        record_error(p.err, kDevTimeoutPeer);
-                        break;
-                    }
-                }
+    // ---- count the pieces (one fence covers both), then merge every unit
+    // whose count this CTA completed: all its pieces are stored and visible
+    // (each contributor fenced before counting - warp 0's stores are ordered
+    // before lane 0's fence by __syncwarp - and the merging CTA fences after
+    // reading the count; its other threads follow through the barrier).
+    // The merge reads the pieces in contributor order, so the result does not
+    // depend on which contributor merges.
+    if (warp == 0) {
+        __syncwarp();
+        if (lane == 0) {
+            int f0 = 0, f1 = 0;
+            if (xm[0] >= 0 || xm[6] >= 0) {
+                fence_acq_rel_gpu();                   // release this CTA's pieces
+                if (xm[0] >= 0) f0 = atom_add_relaxed_gpu(&p.counters[xm[0]], 1) == xm[2] - xm[1];
+                if (xm[6] >= 0) f1 = atom_add_relaxed_gpu(&p.counters[xm[6]], 1) == xm[8] - xm[7];
+                if (f0 | f1) fence_acq_rel_gpu();      // acquire the other contributors' pieces
             }
+            xflag[0] = f0;
+            xflag[1] = f1;
+            FR_TRACE_EV(kEvCounted);
         }
-        consumer_sync(NW * 32);                        // the pieces are visible to every thread
-        merge_pieces<D, NT, NW>(p, xarea, m_cf, m_cl, m_cf_tail, m_gcount, m_head_base);
+    }
+    consumer_sync(NW * 32);
+#pragma unroll 1
+    for (int r = 0; r < 2; ++r) {                      // flags are uniform over the consumer warps
+        if (!xflag[r]) continue;
+        const int* m = xm + 6 * r;
+        const int bb = m[4], jj = m[5];
+        const int kvh = jj / hg, hgrp = jj - (jj / hg) * hg;
+        const int gcount = min(GP, p.G - hgrp * GP);
+        const size_t head_base = (size_t)bb * p.H + kvh * p.G + hgrp * GP;
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvMergeBegin);
+        merge_pieces<D, NT, NW>(p, xarea, m[1], m[2], m[3] != 0, gcount, head_base);
         if (threadIdx.x == 0) {
-            p.counters[m_unit] = 0;                    // every piece was counted: re-arm
+            p.counters[m[0]] = 0;                      // every piece was counted: re-arm
             FR_TRACE_EV(kEvMergeEnd);
         }
     }

@@ -1391,24 +1391,11 @@ int fr_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
 unsigned long long fr_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 #ifdef FR_TRACE
-// Trace builds only (libforgert_b200_trace.so): attach a device buffer of
-// kTraceMaxCtas x kTracePerCta fr::TraceRec records (nullptr detaches),
-// zeroing the per-CTA launch and record counters; fr_trace_fill copies the
-// kTraceMaxCtas record counts to host memory.
+// Trace builds only (libforgert_b200_trace.so): attach a zeroed device
+// buffer of kTraceMaxCtas x kTracePerCta fr::TraceRec records (nullptr
+// detaches).  Every record whose time is non-zero is an event.
 FR_API int fr_trace_attach(void* buf) {
-    void* a = nullptr;
-    void* b = nullptr;
     cudaError_t e = cudaMemcpyToSymbol(fr::fr_trace_buf, &buf, sizeof(buf));
-    if (e == cudaSuccess) e = cudaGetSymbolAddress(&a, fr::fr_trace_launch);
-    if (e == cudaSuccess) e = cudaGetSymbolAddress(&b, fr::fr_trace_fill);
-    if (e == cudaSuccess) e = cudaMemset(a, 0, sizeof(unsigned) * fr::kTraceMaxCtas);
-    if (e == cudaSuccess) e = cudaMemset(b, 0, sizeof(unsigned) * fr::kTraceMaxCtas);
-    return e == cudaSuccess ? FR_OK : cuda_fail(e);
-}
-
-FR_API int fr_trace_fill(unsigned* host_counts) {
-    cudaError_t e = cudaMemcpyFromSymbol(host_counts, fr::fr_trace_fill,
-                                         sizeof(unsigned) * fr::kTraceMaxCtas);
     return e == cudaSuccess ? FR_OK : cuda_fail(e);
 }
 #endif

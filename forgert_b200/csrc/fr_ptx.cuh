@@ -198,9 +198,6 @@ __device__ __forceinline__ void st_dsmem_u32(uint32_t addr, uint32_t v) {
     asm volatile("st.shared::cluster.u32 [%0], %1;" :: "r"(addr), "r"(v) : "memory");
 }
 
-// Atomic add with acquire-release semantics at GPU scope: orders every write
-// this thread has observed (including other threads' writes published to it
-// by a barrier) before the add, and the add before later reads.
 // Release increment (no value returned): publishes the stores this thread
 // has observed (e.g. its warp's, ordered before by __syncwarp).
 __device__ __forceinline__ void red_add_release_gpu(int* addr, int v) {
@@ -213,11 +210,29 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* addr) {
     return v;
 }
 
+// Atomic add with acquire-release semantics at GPU scope: orders every write
+// this thread has observed (including other threads' writes published to it
+// by a barrier) before the add, and the add before later reads.
 __device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
     int old;
     asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;"
                  : "=r"(old) : "l"(addr), "r"(v) : "memory");
     return old;
+}
+
+// Relaxed atomic add at GPU scope (ordering comes from fences around it).
+__device__ __forceinline__ int atom_add_relaxed_gpu(int* addr, int v) {
+    int old;
+    asm volatile("atom.add.relaxed.gpu.global.s32 %0, [%1], %2;"
+                 : "=r"(old) : "l"(addr), "r"(v) : "memory");
+    return old;
+}
+
+// Acquire-release fence at GPU scope.  Unlike __threadfence() (a
+// sequentially consistent fence) it only orders this thread's own accesses:
+// before a relaxed atomic it releases, after one it acquires.
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
 // 8-byte system-scope relaxed store / load.  An aligned 8-byte access is

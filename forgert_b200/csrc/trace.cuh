@@ -4,14 +4,19 @@
 // `python -m forgert_b200.build --trace` -> libforgert_b200_trace.so); in
 // the product library every FR_TRACE_EV(...) compiles to nothing.
 //
-// Each CTA index owns kTracePerCta record slots and two counters: how many
-// launches it has started (its launch ordinal, fixed at the kEvStart event
-// and kept in shared memory for the CTA's later events) and how many records
-// it has written.  A record holds the %globaltimer value (ns), the launch
-// ordinal, the event id and the SM, so launches that overlap in time (the
-// next layer's CTAs start while this layer's still run) stay apart.  The
-// host attaches a buffer with fr_trace_attach (trace builds only);
-// forgert_b200/phase_trace.py turns the records into per-phase times.
+// A record holds the %globaltimer value (ns), the low 32 bits of the grid's
+// launch number (%gridid, unique per launch in a context), the event id and
+// the SM, so launches that overlap in time (the next layer's CTAs start
+// while this layer's still run) stay apart.  Recording costs a timer read,
+// a shared-memory increment and one store that nobody waits for - no
+// global atomics, whose round trips would stretch the phases being timed.
+// Each CTA index owns kTraceLaunches blocks of kTraceEvents records; a
+// launch writes block (gridid mod kTraceLaunches), so the last
+// kTraceLaunches launches of a kernel stay apart.  All events come from
+// thread 0 except the producer's kEvFirstIssue, which takes the block's last
+// record.  The host zeroes the buffer and attaches it with fr_trace_attach
+// (trace builds only); forgert_b200/phase_trace.py reads every record whose
+// time is non-zero.
 #pragma once
 #include <cstdint>
 
@@ -30,36 +35,47 @@ enum TraceEvent : unsigned {
     kEvMergeEnd = 10,    // merge of pieces / clusters done
     kEvXMergeEnd = 11,   // cross-cluster merge (split kernel, last CTA per rank) done
     kEvEnd = 12,         // consumers done
+    kEvCounted = 13,     // pieces counted after the range (persistent kernel)
+    kEvMergeBegin = 14,  // a unit's merge starts (persistent kernel)
+    kEvMergeLoaded = 15, // the merge's first loads have landed (persistent kernel)
 };
 
 constexpr int kTraceMaxCtas = 2048;
-constexpr int kTracePerCta = 4096;
+constexpr int kTraceLaunches = 128;
+constexpr int kTraceEvents = 32;
+constexpr int kTracePerCta = kTraceLaunches * kTraceEvents;
 
 struct TraceRec {
     unsigned long long t;
-    unsigned launch;     // launch ordinal of this CTA index
+    unsigned launch;     // low 32 bits of %gridid
     unsigned ev_sm;      // event | sm << 8
 };
 
 #ifdef FR_TRACE
-__device__ TraceRec* fr_trace_buf = nullptr;          // [kTraceMaxCtas][kTracePerCta]
-__device__ unsigned fr_trace_launch[kTraceMaxCtas];
-__device__ unsigned fr_trace_fill[kTraceMaxCtas];
+__constant__ TraceRec* fr_trace_buf = nullptr;        // [kTraceMaxCtas][kTraceLaunches][kTraceEvents]
 
 __device__ __forceinline__ void trace_event(unsigned ev) {
-    __shared__ unsigned s_launch;
+    __shared__ unsigned s_n;                         // thread 0's records in this launch
     TraceRec* buf = fr_trace_buf;
     if (!buf) return;
     const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
     if (cta >= kTraceMaxCtas) return;
-    unsigned long long t;
+    unsigned long long t, gid;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    asm volatile("mov.u64 %0, %%gridid;" : "=l"(gid));
     unsigned sm;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
-    if (ev == kEvStart) s_launch = atomicAdd(&fr_trace_launch[cta], 1u);
-    const unsigned k = s_launch;
-    const unsigned i = atomicAdd(&fr_trace_fill[cta], 1u);
-    if (i < kTracePerCta) buf[(size_t)cta * kTracePerCta + i] = TraceRec{t, k, ev | (sm << 8)};
+    unsigned i;
+    if (ev == kEvFirstIssue) {
+        i = kTraceEvents - 1;
+    } else {
+        if (ev == kEvStart) s_n = 0;
+        i = s_n;
+        if (i >= kTraceEvents - 1) return;
+        s_n = i + 1;
+    }
+    const size_t blk = (size_t)cta * kTraceLaunches + (size_t)(gid % kTraceLaunches);
+    buf[blk * kTraceEvents + i] = TraceRec{t, (unsigned)gid, ev | (sm << 8)};
 }
 #define FR_TRACE_EV(ev) ::fr::trace_event(ev)
 #else

@@ -37,7 +37,8 @@ import numpy as np
 PKG = Path(__file__).resolve().parent
 EVENTS = {1: "start", 2: "meta", 3: "first_issue", 4: "dep_wait", 5: "q_loaded",
           6: "first_full", 7: "loop_end", 8: "fold", 9: "stored", 10: "merge_end",
-          11: "xmerge_end", 12: "end"}
+          11: "xmerge_end", 12: "end", 13: "counted", 14: "merge_begin",
+          15: "merge_loaded"}
 
 
 def parse(argv=None):
@@ -50,12 +51,14 @@ def parse(argv=None):
     ap.add_argument("--no-overlap", action="store_true")
     ap.add_argument("--gemm", action="store_true")
     ap.add_argument("--dump", default=None, help="also save the raw records (.npz, one array per CTA)")
+    ap.add_argument("--lib", default=None,
+                    help="trace build to load (default: libforgert_b200_trace.so, built if missing)")
     return ap.parse_args(argv)
 
 
-def load_trace_lib():
+def load_trace_lib(path=None):
     from . import build as B
-    path = B.TRACE_LIB_PATH
+    path = Path(path) if path else B.TRACE_LIB_PATH
     if not path.exists():
         B.build(trace=True)
     os.environ["FORGERT_B200_LIB"] = str(path)
@@ -63,13 +66,23 @@ def load_trace_lib():
     lib = _lib.load()
     lib.fr_trace_attach.restype = ctypes.c_int
     lib.fr_trace_attach.argtypes = [ctypes.c_void_p]
-    lib.fr_trace_fill.restype = ctypes.c_int
-    lib.fr_trace_fill.argtypes = [ctypes.c_void_p]
     return lib
 
 
-MAX_CTAS, PER_CTA = 2048, 4096          # kTraceMaxCtas, kTracePerCta (csrc/trace.cuh)
+MAX_CTAS, PER_CTA = 2048, 128 * 32      # kTraceMaxCtas, kTraceLaunches x kTraceEvents (csrc/trace.cuh)
+# launch = low 32 bits of the grid's %gridid (one value per launch)
 REC = np.dtype([("t", "<u8"), ("launch", "<u4"), ("ev_sm", "<u4")])
+
+
+def records_by_cta(raw: np.ndarray) -> dict:
+    """raw: the attached buffer as [MAX_CTAS, PER_CTA] records.  Returns
+    {cta: its non-empty records in time order}."""
+    out = {}
+    for c in range(raw.shape[0]):
+        r = raw[c][raw[c]["t"] != 0]
+        if r.size:
+            out[c] = np.sort(r, order="t")
+    return out
 
 
 def build_cfg2(torch, args, A, dev):
@@ -107,10 +120,12 @@ def build_cfg3(torch, args, A, dev):
 
 
 def summarise(per_cta):
-    """per_cta: {cta: records (t, launch, ev_sm)}.  For each launch ordinal,
+    """per_cta: {cta: records (t, launch, ev_sm)}.  For each launch,
     phases are timed from the launch's earliest CTA start; reported as the
     median over launches of the median CTA (first occurrence of the event in
-    the CTA) and of the latest CTA (last occurrence)."""
+    the CTA), of the median CTA's last occurrence (per-item events of the
+    persistent kernel: the end of its range) and of the latest CTA (last
+    occurrence)."""
     launches: dict[int, dict[str, dict[int, list]]] = {}
     for cta, recs in per_cta.items():
         for t, k, evsm in zip(recs["t"], recs["launch"], recs["ev_sm"]):
@@ -126,8 +141,9 @@ def summarise(per_cta):
         for name, by_cta in d.items():
             first = np.array([min(v) for v in by_cta.values()], np.float64) - t0
             last = np.array([max(v) for v in by_cta.values()], np.float64) - t0
-            ph = phases.setdefault(name, {"med": [], "latest": [], "ctas": []})
+            ph = phases.setdefault(name, {"med": [], "med_last": [], "latest": [], "ctas": []})
             ph["med"].append(float(np.median(first)))
+            ph["med_last"].append(float(np.median(last)))
             ph["latest"].append(float(last.max()))
             ph["ctas"].append(len(by_cta))
     period = np.diff(np.array(starts, np.float64))
@@ -136,6 +152,7 @@ def summarise(per_cta):
     for name in [v for v in EVENTS.values() if v in phases]:
         ph = phases[name]
         out[name] = {"median_cta_us": round(statistics.median(ph["med"]) / 1e3, 3),
+                     "median_cta_last_us": round(statistics.median(ph["med_last"]) / 1e3, 3),
                      "latest_cta_us": round(statistics.median(ph["latest"]) / 1e3, 3),
                      "ctas": int(statistics.median(ph["ctas"]))}
     return out
@@ -143,7 +160,7 @@ def summarise(per_cta):
 
 def main(argv=None):
     args = parse(argv)
-    lib = load_trace_lib()
+    lib = load_trace_lib(args.lib)
     import torch
     from . import attention as A
     dev = torch.device("cuda", 0)
@@ -175,18 +192,17 @@ def main(argv=None):
     torch.cuda.synchronize()
     buf = torch.zeros(MAX_CTAS * PER_CTA * REC.itemsize, dtype=torch.uint8, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
     assert lib.fr_trace_attach(buf.data_ptr()) == 0
     with torch.cuda.stream(stream):
         for i in range(args.replays):
             flush.fill_(i)
             g.replay()
     torch.cuda.synchronize()
-    fill = np.zeros(MAX_CTAS, np.uint32)
-    assert lib.fr_trace_fill(fill.ctypes.data) == 0
     lib.fr_trace_attach(None)
     allrec = np.frombuffer(buf.cpu().numpy().tobytes(), dtype=REC).reshape(MAX_CTAS, PER_CTA)
-    per_cta = {c: allrec[c, :min(int(fill[c]), PER_CTA)] for c in range(MAX_CTAS) if fill[c]}
-    n = int(sum(min(int(f), PER_CTA) for f in fill))
+    per_cta = records_by_cta(allrec)
+    n = int(sum(r.size for r in per_cta.values()))
     res = summarise(per_cta)
     if args.dump:
         np.savez_compressed(args.dump, **{f"cta{c}": r for c, r in per_cta.items()})

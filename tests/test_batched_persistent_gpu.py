@@ -205,3 +205,16 @@ def test_split_grid_selected_by_environment(tmp_path):
     ks = [W.normal_fp16(rng, (n, 4, 128)) for n in lens]
     vs = [W.normal_fp16(rng, (n, 4, 128)) for n in lens]
     assert_close(np.load(f), O.batched_f64(q, ks, vs, lens), what="split grid")
+
+
+def test_bitwise_repeatable():
+    """The contributor that completes a unit's count merges it, and which one
+    that is varies from call to call; the merge reads the pieces in a fixed
+    order, so repeated calls give identical bits."""
+    rng = np.random.default_rng(18)
+    lens = rng.integers(1024, 8193, size=32)
+    q, ks, vs, pk, pv, offs, rows = make_batch(19, 28, 4, 128, lens)
+    first = run(q, pk, pv, offs, lens, rows)
+    for _ in range(4):
+        assert np.array_equal(run(q, pk, pv, offs, lens, rows), first)
+    assert_close(first, O.batched_f64(q, ks, vs, lens), what="repeatable batch")
