@@ -291,20 +291,26 @@ __device__ __forceinline__ void consume_tile(uint32_t kst, uint32_t vst, unsigne
         fenced = true;
     }
 
-    // ---- S^T = K Q^T (16 positions x GP heads)
-    float sacc[NT][4];
+    // ---- S^T = K Q^T (16 positions x GP heads).  Even and odd k-steps
+    // accumulate separately: two dependent MMA chains of half the length
+    // (one warp per sub-partition has nothing else to hide the latency with).
+    float sacc[NT][4], sodd[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
+        for (int c = 0; c < 4; ++c) sacc[nt][c] = sodd[nt][c] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < KSTEPS; ++ks) {
         uint32_t a0, a1, a2, a3;
         ldsm_x4(a0, a1, a2, a3, kst + swz_offset<TILE>(k_row, ks * 16 + k_col));
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
-            mma_16816(sacc[nt], a0, a1, a2, a3, qb[ks][nt][0], qb[ks][nt][1]);
+            mma_16816((ks & 1) ? sodd[nt] : sacc[nt], a0, a1, a2, a3, qb[ks][nt][0], qb[ks][nt][1]);
     }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sacc[nt][c] += sodd[nt][c];
 
     // ---- mask rows past the end
     const bool row_lo_ok = g < valid_rows;
@@ -665,6 +671,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         // Every consumer must be past its last ldmatrix before the ring is
         // reused as the merge area.
         const int ok_all = consumer_sync_and(ok ? 1 : 0, NW * 32);
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvFoldSynced);
 
         // ---- cross-warp merge through shared memory -> CTA state
         constexpr int MS = S::kMergeStride;
@@ -693,6 +700,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                     }
             }
         }
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvFoldStored);
         consumer_sync(NW * 32);
         // One thread per (head, warp), NW adjacent lanes per head: the max
         // over warps and the weighted l by shuffles, each warp's weight.
@@ -717,6 +725,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
             }
         }
         consumer_sync(NW * 32);
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvFoldWeights);
 
         const size_t head_base = (size_t)b * p.H + h0;
         constexpr int kPerThread = GP * D / (NW * 32);
@@ -756,6 +765,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     if (threadIdx.x == 0) FR_TRACE_EV(kEvFold);
     if (!p.counters) return;       // unfused / single-split paths end here (uniform)
     __syncthreads();               // CTA state complete (producer included)
+    if (threadIdx.x == 0) FR_TRACE_EV(kEvStateDone);
 
     // ------------------------------------------------------ fused merge
     // Level 1: the CL CTAs of the cluster merge their states through DSMEM;
@@ -798,6 +808,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         // Push: message [m GP][l GP][acc slice j] to every cluster rank j,
         // stored at [my rank] of its receive area.
         cluster_wait_acquire();                      // every recv_bar is initialised
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvClusterReady);
         const int chunks = x_msg / 4;
         const uint32_t recv_s = smem_u32(recv), bar_s = smem_u32(recv_bar);
         for (int idx = threadIdx.x; idx < CL * chunks; idx += blockDim.x) {
@@ -816,6 +827,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
                         dsmem_addr(bar_s, uint32_t(j)));
         }
         if (!mbar_wait_bounded(recv_bar, 0)) record_error(p.err, kDevTimeoutFull);
+        if (threadIdx.x == 0) FR_TRACE_EV(kEvRecvDone);
     }
     {
         for (int e = e_begin + threadIdx.x; e < e_end; e += blockDim.x) {

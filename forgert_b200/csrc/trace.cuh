@@ -38,6 +38,12 @@ enum TraceEvent : unsigned {
     kEvCounted = 13,     // pieces counted after the range (persistent kernel)
     kEvMergeBegin = 14,  // a unit's merge starts (persistent kernel)
     kEvMergeLoaded = 15, // the merge's first loads have landed (persistent kernel)
+    kEvFoldSynced = 16,  // consumer warps past their last tile (split kernel)
+    kEvStateDone = 17,   // CTA state complete, whole CTA synchronised (split kernel)
+    kEvClusterReady = 18,// cluster barrier passed, pushes start (split kernel)
+    kEvRecvDone = 19,    // every cluster rank's message received (split kernel)
+    kEvFoldStored = 20,  // thread 0's accumulator fragments stored for the fold (split kernel)
+    kEvFoldWeights = 21, // per-warp fold weights known (split kernel)
 };
 
 constexpr int kTraceMaxCtas = 2048;

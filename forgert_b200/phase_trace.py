@@ -38,7 +38,8 @@ PKG = Path(__file__).resolve().parent
 EVENTS = {1: "start", 2: "meta", 3: "first_issue", 4: "dep_wait", 5: "q_loaded",
           6: "first_full", 7: "loop_end", 8: "fold", 9: "stored", 10: "merge_end",
           11: "xmerge_end", 12: "end", 13: "counted", 14: "merge_begin",
-          15: "merge_loaded"}
+          15: "merge_loaded", 16: "fold_synced", 17: "state_done", 18: "cluster_ready",
+          19: "recv_done", 20: "fold_stored", 21: "fold_weights"}
 
 
 def parse(argv=None):
