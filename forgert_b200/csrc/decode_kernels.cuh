@@ -291,26 +291,20 @@ __device__ __forceinline__ void consume_tile(uint32_t kst, uint32_t vst, unsigne
         fenced = true;
     }
 
-    // ---- S^T = K Q^T (16 positions x GP heads).  Even and odd k-steps
-    // accumulate separately: two dependent MMA chains of half the length
-    // (one warp per sub-partition has nothing else to hide the latency with).
-    float sacc[NT][4], sodd[NT][4];
+    // ---- S^T = K Q^T (16 positions x GP heads)
+    float sacc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) sacc[nt][c] = sodd[nt][c] = 0.f;
+        for (int c = 0; c < 4; ++c) sacc[nt][c] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < KSTEPS; ++ks) {
         uint32_t a0, a1, a2, a3;
         ldsm_x4(a0, a1, a2, a3, kst + swz_offset<TILE>(k_row, ks * 16 + k_col));
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
-            mma_16816((ks & 1) ? sodd[nt] : sacc[nt], a0, a1, a2, a3, qb[ks][nt][0], qb[ks][nt][1]);
+            mma_16816(sacc[nt], a0, a1, a2, a3, qb[ks][nt][0], qb[ks][nt][1]);
     }
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) sacc[nt][c] += sodd[nt][c];
 
     // ---- mask rows past the end
     const bool row_lo_ok = g < valid_rows;
