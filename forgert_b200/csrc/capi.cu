@@ -59,6 +59,7 @@ struct DeviceState {
     int persist_occ[4] = {0};    // CTAs/SM of the persistent batched kernels
     int resident[4][5] = {{-1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1},
                           {-1, -1, -1, -1, -1}};   // co-resident clusters per (slot, log2 size)
+    int resident_g[4][2] = {{-1, -1}, {-1, -1}, {-1, -1}, {-1, -1}};   // grouped form, 8 / 16
 };
 
 std::mutex g_mu;
@@ -175,16 +176,40 @@ auto kernel_ptr() {
 template <int D, int NT>
 using SmemOf = fr::SplitSmem<D, NT, kTile, Stages<D>::value, kConsumerWarps>;
 
+// Grouped form of the fused single-sequence kernel: two groups of four
+// consumer warps take alternate tiles (each group owns half the ring's
+// stages: 4 at D=128, one CTA per SM), so a CTA consumes its prefetched
+// tiles at twice the rate.  Used for small grids (at most one CTA per two
+// SMs, the next call's CTAs fitting on the other SMs) of at least two tiles
+// per CTA, with clusters of 8 or 16.
+template <int D> struct StagesG;
+template <> struct StagesG<64> { static constexpr int value = 6; };
+template <> struct StagesG<128> { static constexpr int value = 4; };
+constexpr int kGroupedWarps = 2 * kConsumerWarps;
+
+template <int D, int NT, int CL>
+auto kernel_ptr_g() {
+    return fr::split_decode_kernel<D, NT, kTile, StagesG<D>::value, kGroupedWarps, CL, false>;
+}
+
+template <int D, int NT>
+using SmemOfG = fr::SplitSmem<D, NT, kTile, StagesG<D>::value, kGroupedWarps>;
+
 template <int D, int NT, int CL>
 int set_smem_attr() {
-    for (auto fn : {kernel_ptr<D, NT, CL, false>(), kernel_ptr<D, NT, CL, true>()}) {
+    auto set = [](auto fn, size_t bytes) -> int {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(SmemOf<D, NT>::kBytes));
+                                             static_cast<int>(bytes));
         if (e == cudaSuccess && CL > 8)        // 16-CTA clusters are a non-portable size
             e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return cuda_fail(e);
+        return e == cudaSuccess ? FR_OK : cuda_fail(e);
+    };
+    int rc = set(kernel_ptr<D, NT, CL, false>(), SmemOf<D, NT>::kBytes);
+    if (rc == FR_OK) rc = set(kernel_ptr<D, NT, CL, true>(), SmemOf<D, NT>::kBytes);
+    if constexpr (CL >= 8) {
+        if (rc == FR_OK) rc = set(kernel_ptr_g<D, NT, CL>(), SmemOfG<D, NT>::kBytes);
     }
-    return FR_OK;
+    return rc;
 }
 
 // Guards the per-device attribute bits, occupancy and co-residency caches:
@@ -241,6 +266,79 @@ int launch_split(const DecodeParams& p, dim3 grid, cudaStream_t s, bool pdl) {
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return FR_OK;
+}
+
+// Co-resident clusters of 8 or 16 CTAs of the grouped form (cached).
+int resident_clusters_g(int D, int nt, int cl, DeviceState* st) {
+    const int slot = (D == 64 ? 0 : 2) + (nt - 1);
+    std::lock_guard<std::mutex> lk(g_prep_mu);
+    int& cached = st->resident_g[slot][cl == 16 ? 1 : 0];
+    if (cached >= 0) return cached;
+    const void* fn = nullptr;
+    size_t smem = 0;
+    if (D == 64) {
+        fn = nt == 1 ? (cl == 16 ? (const void*)kernel_ptr_g<64, 1, 16>() : (const void*)kernel_ptr_g<64, 1, 8>())
+                     : (cl == 16 ? (const void*)kernel_ptr_g<64, 2, 16>() : (const void*)kernel_ptr_g<64, 2, 8>());
+        smem = nt == 1 ? SmemOfG<64, 1>::kBytes : SmemOfG<64, 2>::kBytes;
+    } else {
+        fn = nt == 1 ? (cl == 16 ? (const void*)kernel_ptr_g<128, 1, 16>() : (const void*)kernel_ptr_g<128, 1, 8>())
+                     : (cl == 16 ? (const void*)kernel_ptr_g<128, 2, 16>() : (const void*)kernel_ptr_g<128, 2, 8>());
+        smem = nt == 1 ? SmemOfG<128, 1>::kBytes : SmemOfG<128, 2>::kBytes;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, cl, 1);
+    cfg.blockDim = dim3(32 * (kGroupedWarps + 1), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = cl;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n < 0) {
+        cudaGetLastError();
+        n = 0;
+    }
+    cached = n;
+    return n;
+}
+
+// The grouped form (clusters of 8 or 16, contiguous caches).
+template <int D, int NT, int CL>
+int launch_split_g(const DecodeParams& p, dim3 grid, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(32 * (kGroupedWarps + 1), 1, 1);
+    cfg.dynamicSmemBytes = SmemOfG<D, NT>::kBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attrs[2];
+    unsigned n = 0;
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = 1;
+    attrs[n].val.clusterDim.y = CL;
+    attrs[n].val.clusterDim.z = 1;
+    ++n;
+    if (pdl) {
+        attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = n;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel_ptr_g<D, NT, CL>(), p);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    return FR_OK;
+}
+
+template <int D>
+int launch_grouped(const DecodeParams& p, int nt, int cl, dim3 grid, cudaStream_t s, bool pdl) {
+    if (nt == 1)
+        return cl == 16 ? launch_split_g<D, 1, 16>(p, grid, s, pdl) : launch_split_g<D, 1, 8>(p, grid, s, pdl);
+    return cl == 16 ? launch_split_g<D, 2, 16>(p, grid, s, pdl) : launch_split_g<D, 2, 8>(p, grid, s, pdl);
 }
 
 template <int D, int NT, bool PAGED>
@@ -686,11 +784,25 @@ int run_decode(DecodeParams p, int head_dim, int batch, int max_kv_len, __half* 
         }
     }
     dim3 grid(p.Hkv * pl.head_groups, splits, batch);
+    // Grouped consumers (two tiles at a time per CTA): a fused single-sequence
+    // call on contiguous caches, clusters of 8 or 16, at least two tiles per
+    // CTA, and a grid of at most one CTA per two SMs (FORGERT_GROUPED, read
+    // once: 0 = never, 2 = whatever the grid size).
+    static const int grouped_on = env_int("FORGERT_GROUPED", 1);
+    const long long ctas = (long long)grid.x * grid.y * grid.z;
+    const bool grouped = grouped_on && waves == 1 && p.counters && !p.block_table &&
+                         p.xworld == 0 && (cl == 8 || cl == 16) &&
+                         pl.split_len >= 2 * kTile && (grouped_on == 2 || 2 * ctas <= st->sm_count) &&
+                         (long long)resident_clusters_g(D, pl.nt, cl, st) * cl >= ctas;
     static const int trace_plan = env_int("FORGERT_TRACE_PLAN", 0);
     if (trace_plan)
         std::fprintf(stderr, "[forgert] plan D=%d batch=%d units=%lld splits=%d split_len=%d "
-                     "cluster=%d fused=%d xworld=%d grid=(%u,%u,%u)\n", D, batch, units, splits,
-                     pl.split_len, cl, (int)fused, p.xworld, grid.x, grid.y, grid.z);
+                     "cluster=%d fused=%d xworld=%d grouped=%d grid=(%u,%u,%u)\n", D, batch,
+                     units, splits, pl.split_len, cl, (int)fused, p.xworld, (int)grouped, grid.x,
+                     grid.y, grid.z);
+    if (grouped)
+        return D == 64 ? launch_grouped<64>(p, pl.nt, cl, grid, s, pdl)
+                       : launch_grouped<128>(p, pl.nt, cl, grid, s, pdl);
     rc = D == 64 ? launch_split_any<64>(p, pl.nt, cl, grid, s, pdl)
                  : launch_split_any<128>(p, pl.nt, cl, grid, s, pdl);
     if (rc != FR_OK || p.write_final || p.counters) return rc;

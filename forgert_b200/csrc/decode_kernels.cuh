@@ -373,7 +373,8 @@ __device__ __forceinline__ void consume_tile(uint32_t kst, uint32_t vst, unsigne
 // ---------------------------------------------------------------------------
 // Split-KV decode kernel.
 //   grid  = (Hkv * head_groups, num_splits, B), clusters of CL CTAs along y
-//   block = 32 * (NW + 1): NW consumer warps + 1 producer warp
+//   block = 32 * (NW + 1): NW consumer warps + 1 producer warp (NW = 8 with
+//   TILE = 64: two groups of four warps taking alternate tiles)
 //
 // Output paths (chosen by the host, uniform over the grid):
 //   write_final        one split: the CTA writes fp16 out directly;
@@ -396,7 +397,14 @@ template <int D, int NT, int TILE, int STAGES, int NW, int CL, bool PAGED>
 __global__ void __launch_bounds__(32 * (NW + 1))
 split_decode_kernel(const __grid_constant__ DecodeParams p) {
     static_assert(D % 64 == 0, "head_dim must be a multiple of 64");
-    static_assert(TILE == 16 * NW, "each consumer warp owns one 16-row m-tile per stage");
+    // Consumer groups: NW warps of 16 rows each cover GR tiles at a time;
+    // with GR = 2 the two groups of NW/2 warps take alternate tiles (group g
+    // tiles g, g + 2, ...), so each group owns the stages s = g mod 2 of the
+    // ring and never waits on a stage the other group consumes.
+    constexpr int GR = 16 * NW / TILE;
+    constexpr int WPG = NW / GR;                     // warps per group
+    static_assert(GR * TILE == 16 * NW && (GR == 1 || GR == 2) && STAGES % GR == 0,
+                  "each consumer warp owns one 16-row m-tile of its group's tiles");
     static_assert(CL >= 1 && CL <= 16, "cluster size");
     using S = SplitSmem<D, NT, TILE, STAGES, NW>;
     constexpr int GP = NT * 8;          // padded heads per CTA
@@ -455,7 +463,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NW);
+            mbar_init(&empty[s], WPG);               // one group consumes each stage
         }
         mbar_init(recv_bar, 1);
         if (cluster_merge) mbar_arrive_expect_tx(recv_bar, uint32_t(CL * x_msg * 4));
@@ -628,11 +636,12 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         }
 
         const float sl2 = p.scale_log2;
-        const int row0 = warp * 16;          // this warp's 16 rows of every tile
+        const int grp = warp / WPG;          // this warp's group: tiles grp, grp + GR, ...
+        const int row0 = (warp - grp * WPG) * 16;   // its 16 rows of each of those tiles
         const uint32_t kring_s = smem_u32(kring);
         const uint32_t vring_s = smem_u32(vring);
 
-        for (int i = 0; i < ntiles; ++i) {
+        for (int i = grp; i < ntiles; i += GR) {
             const int s = i % STAGES;
             if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1)) {
                 record_error(p.err, kDevTimeoutFull);

@@ -431,3 +431,65 @@ def test_overlap_mode_after_rope_append(use_graph):
                                            ct, st, kv - 1)
         exact = O.decode_f64(qo[0], kco, vco, kv)
         assert_close(outs[l].cpu().numpy(), exact, what=f"overlap layer {l}")
+
+
+_GROUPED_PROCESS = r"""
+import json, sys
+sys.path.insert(0, sys.argv[1])
+import numpy as np, torch
+from forgert_b200 import attention as A, _lib, workloads as W
+lib = _lib.load()
+lib.fr_set_launch_overlap(1)
+s = torch.cuda.Stream()
+outs = {}
+for (H, Hkv, D, T) in json.loads(sys.argv[3]):
+    rng = np.random.default_rng(T + 7 * H + D)
+    q = W.normal_fp16(rng, (H, D)); k = W.normal_fp16(rng, (T, Hkv, D)); v = W.normal_fp16(rng, (T, Hkv, D))
+    d = lambda a: torch.from_numpy(a).cuda()
+    qd, kd, vd = d(q), d(k), d(v)
+    out = torch.full_like(qd, float("nan"))
+    with torch.cuda.stream(s):
+        for _ in range(3):                       # chained calls (launch overlap on a stream)
+            A.decode_attn_v4_flash(qd, kd, vd, out, H, Hkv, D, T, s)
+    torch.cuda.synchronize()
+    outs[f"{H}_{Hkv}_{D}_{T}"] = out.cpu().numpy()
+np.savez(sys.argv[2], **outs)
+print(json.dumps({"err": A.device_error()}))
+"""
+
+_GROUPED_CASES = [(12, 2, 128, 1025), (12, 2, 128, 2048), (12, 2, 128, 4096), (12, 2, 128, 4097),
+                  (28, 4, 128, 3000), (14, 2, 64, 2048), (32, 2, 128, 4096), (40, 2, 64, 1500)]
+
+
+@pytest.mark.parametrize("grouped", ["1", "0"])
+def test_grouped_consumers(tmp_path, grouped):
+    """Single-sequence calls of a few thousand positions run the kernel form
+    with two consumer groups taking alternate tiles (FORGERT_GROUPED, read
+    once per process, default on); with it off they run the four-warp form.
+    Both match the oracle, on a stream with launch overlap, and the plan trace
+    shows which form ran."""
+    import json
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, FORGERT_GROUPED=grouped, FORGERT_TRACE_PLAN="1")
+    f = tmp_path / "out.npz"
+    r = subprocess.run([sys.executable, "-c", _GROUPED_PROCESS, str(root), str(f),
+                        json.dumps(_GROUPED_CASES)], env=env, capture_output=True, text=True,
+                       timeout=600, cwd=str(root))
+    assert r.returncode == 0, r.stderr[-3000:]
+    assert json.loads(r.stdout.strip().splitlines()[-1])["err"] == 0
+    plans = [ln for ln in r.stderr.splitlines() if "[forgert] plan" in ln]
+    assert plans and any(f"grouped={grouped}" in ln for ln in plans)
+    if grouped == "0":
+        assert not any("grouped=1" in ln for ln in plans)
+    outs = np.load(f)
+    for (H, Hkv, D, T) in _GROUPED_CASES:
+        rng = np.random.default_rng(T + 7 * H + D)
+        q = W.normal_fp16(rng, (H, D))
+        k = W.normal_fp16(rng, (T, Hkv, D))
+        v = W.normal_fp16(rng, (T, Hkv, D))
+        assert_close(outs[f"{H}_{Hkv}_{D}_{T}"], O.decode_f64(q, k, v),
+                     what=f"grouped={grouped} H{H} Hkv{Hkv} D{D} T{T}")
