@@ -107,8 +107,8 @@ struct DecodeParams {
 };
 
 // Layout of one rank's exchange buffer (bytes from its base):
-//   [0, 256)   header: u32 epoch (calls completed), u32 done (CTAs of the
-//              current call that finished)
+//   [0, 256)   header: u32 epoch (calls completed), u32 count (CTAs of the
+//              current call that have read the epoch)
 //   then ml  [2 parities][world][rows][2] u64 words
 //   then acc [2 parities][world][rows][D] u64 words
 // Every word is (epoch of the call that wrote it) << 32 | fp32 bits, stored
@@ -477,6 +477,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     const int t = lane & 3;      // fragment column pair
     float o[DTILES][NT][4];
     float m_run[NT][2], l_run[NT][2];
+    uint32_t xe_loaded = 0;          // exchange header (calls completed), read after the wait
 
     if (PAGED && warp == NW) {
         // -------------------------------------------------- paged producer
@@ -603,6 +604,9 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         if (warp == 0 && lane < (gcount * D * 2 + 127) / 128)
             prefetch_l2(p.q + ((size_t)b * p.H + h0) * D + lane * 64);
         grid_dependency_wait();
+        // The exchange epoch: every call's last CTA advances it before the
+        // grid ends, so it is final here; read now, used at the merge.
+        if (p.xworld > 0 && threadIdx.x == 0) xe_loaded = __ldcg(XLayout::header(p.xbuf[p.xrank]));
         if (threadIdx.x == 0) FR_TRACE_EV(kEvDepWait);
 
         // Q^T as the B operand of S^T = K Q^T: b0 = Q[head][ks*16 + 2t .. +1], b1 = +8.
@@ -767,6 +771,14 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
 
     if (threadIdx.x == 0) FR_TRACE_EV(kEvFold);
     if (!p.counters) return;       // unfused / single-split paths end here (uniform)
+    if (threadIdx.x == 0) {
+        st_flag[1] = xe_loaded;    // (the ring is free once every tile is consumed)
+        // Exchange: count this CTA as having read the epoch (the release
+        // orders the read before the count); the first CTA advances the
+        // epoch for the next call once every CTA is counted.
+        if (p.xworld > 0)
+            red_add_release_gpu(reinterpret_cast<int*>(XLayout::header(p.xbuf[p.xrank]) + 1), 1);
+    }
     __syncthreads();               // CTA state complete (producer included)
     if (threadIdx.x == 0) FR_TRACE_EV(kEvStateDone);
 
@@ -789,7 +801,7 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
     // Cross-GPU exchange: this call's epoch (the header advances only after
     // every CTA of the grid has finished) selects the buffer parity.
     const bool xmode = p.xworld > 0;
-    const uint32_t xepoch = xmode ? __ldcg(XLayout::header(p.xbuf[p.xrank])) + 1u : 0u;
+    const uint32_t xepoch = xmode ? st_flag[1] + 1u : 0u;
     const int xpar = int(xepoch & 1u);
     // Stores one element of a final state into every rank's exchange buffer
     // (tagged words, see XLayout).
@@ -982,21 +994,25 @@ split_decode_kernel(const __grid_constant__ DecodeParams p) {
         }
         if (!ok) record_error(p.err, kDevTimeoutPeer);
     }
-    if (xmode) {
-        // The last CTA of the grid to get here advances the epoch; every CTA
-        // read it above (ordered before its count by the barrier and fence).
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            uint32_t* hdr = XLayout::header(p.xbuf[p.xrank]);
-            const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
-            if (atomicAdd(&hdr[1], 1u) == total - 1) {
-                __threadfence();
-                hdr[1] = 0u;
-                hdr[0] = xepoch;
-                __threadfence();
+    if (xmode && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+        // The first CTA advances the epoch once every CTA of the grid has read
+        // it (all of them counted themselves right after their tiles; the grid
+        // is co-resident, so the count completes); the next call reads it after
+        // this grid has ended.  The other CTAs leave without waiting.
+        uint32_t* hdr = XLayout::header(p.xbuf[p.xrank]);
+        const int total = int(gridDim.x * gridDim.y * gridDim.z);
+        int* cnt = reinterpret_cast<int*>(hdr + 1);
+        if (ld_acquire_gpu(cnt) < total) {
+            const unsigned long long t0 = globaltimer_ns();
+            while (ld_acquire_gpu(cnt) < total) {
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    record_error(p.err, kDevTimeoutPeer);
+                    break;
+                }
             }
         }
+        hdr[1] = 0u;
+        hdr[0] = xepoch;
     }
 }
 
