@@ -393,8 +393,12 @@ __device__ __forceinline__ void consume_tile(uint32_t kst, uint32_t vst, unsigne
 // (griddepcontrol.wait) before it reads q or writes anything; K/V tiles of
 // rows below prefetch_rows may stream in before that wait.
 // ---------------------------------------------------------------------------
+// Launch bounds: the four-warp form leaves the register budget to the
+// compiler (its choice, 94-162 registers by instantiation, is what was
+// tuned); the eight-warp form runs one CTA per SM and is told so - left to
+// itself the compiler aimed at three CTAs per SM and spilled.
 template <int D, int NT, int TILE, int STAGES, int NW, int CL, bool PAGED>
-__global__ void __launch_bounds__(32 * (NW + 1))
+__global__ void __launch_bounds__(32 * (NW + 1), NW > 4 ? 1 : 0)
 split_decode_kernel(const __grid_constant__ DecodeParams p) {
     static_assert(D % 64 == 0, "head_dim must be a multiple of 64");
     // Consumer groups: NW warps of 16 rows each cover GR tiles at a time;
