@@ -543,7 +543,7 @@ int query_resident_clusters(int D, int nt, int cl, DeviceState* st) {
 // FORGERT_BATCHED_KERNEL=split selects the split kernel's grid instead
 // (read once).  FORGERT_PERSIST_CTAS_PER_SM caps the CTAs per SM of the
 // persistent grid (default: as many as fit); FORGERT_PERSIST_MIN_TILES
-// (default 16, 0 = off) is the fewest tiles per CTA the kernel aims for
+// (default 8, 0 = off) is the fewest tiles per CTA the kernel aims for
 // before it leaves CTAs idle (never fewer than one CTA per SM).
 template <int D, int NT>
 using PersistOf = fr::PersistSmem<D, NT, kTile, Stages<D>::value, kConsumerWarps>;
@@ -668,7 +668,7 @@ int run_persistent(DecodeParams p, int head_dim, int batch, int max_kv_len, __ha
     p.evict_normal = evict_normal;
     const bool pdl = s != nullptr;
     p.prefetch_meta = (pdl && g_overlap.load(std::memory_order_relaxed)) ? 1 : 0;
-    static const int min_tiles = env_int("FORGERT_PERSIST_MIN_TILES", 16);
+    static const int min_tiles = env_int("FORGERT_PERSIST_MIN_TILES", 8);
     p.min_tiles_per_cta = std::max(0, min_tiles);
     p.min_ctas = st->sm_count;
     // Partition cost of starting an item and of merging a unit, in tile
