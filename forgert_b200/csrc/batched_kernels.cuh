@@ -25,7 +25,7 @@
 // 0,1 -> 0).  Warp 0 then writes the normalised fp16 output (whole unit) or
 // stores the piece's (m, l, acc) state in the CTA's partial slot (2c for
 // its first item, 2c + 1 for its last); the pieces are counted on their
-// units' counters after the range (one fence, then an atomic per piece).
+// units' counters after the range (a release atomic per piece).
 // The contributor whose count completes a unit merges it after its own range
 // (log-sum-exp merge of the pieces in contributor order - the result does
 // not depend on who merges - and re-arm): no CTA ever waits for another.
@@ -623,11 +623,11 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
         if (threadIdx.x == 0) FR_TRACE_EV(kEvStored);
     }
 
-    // ---- count the pieces (one fence covers both), then merge every unit
-    // whose count this CTA completed: all its pieces are stored and visible
-    // (each contributor fenced before counting - warp 0's stores are ordered
-    // before lane 0's fence by __syncwarp - and the merging CTA fences after
-    // reading the count; its other threads follow through the barrier).
+    // ---- count the pieces, then merge every unit whose count this CTA
+    // completed: all its pieces are stored and visible (each contributor
+    // counts with release semantics - warp 0's stores are ordered before lane
+    // 0's count by __syncwarp - and the merging CTA fences after reading the
+    // count; its other threads follow through the barrier).
     // The merge reads the pieces in contributor order, so the result does not
     // depend on which contributor merges.
     if (warp == 0) {
@@ -635,9 +635,9 @@ persistent_decode_kernel(const __grid_constant__ DecodeParams p) {
         if (lane == 0) {
             int f0 = 0, f1 = 0;
             if (xm[0] >= 0 || xm[6] >= 0) {
-                fence_acq_rel_gpu();                   // release this CTA's pieces
-                if (xm[0] >= 0) f0 = atom_add_relaxed_gpu(&p.counters[xm[0]], 1) == xm[2] - xm[1];
-                if (xm[6] >= 0) f1 = atom_add_relaxed_gpu(&p.counters[xm[6]], 1) == xm[8] - xm[7];
+                // each count releases this CTA's pieces
+                if (xm[0] >= 0) f0 = atom_add_release_gpu(&p.counters[xm[0]], 1) == xm[2] - xm[1];
+                if (xm[6] >= 0) f1 = atom_add_release_gpu(&p.counters[xm[6]], 1) == xm[8] - xm[7];
                 if (f0 | f1) fence_acq_rel_gpu();      // acquire the other contributors' pieces
             }
             xflag[0] = f0;

@@ -220,6 +220,15 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
     return old;
 }
 
+// Atomic add with release semantics at GPU scope (orders this thread's
+// earlier accesses, and those a barrier ordered before it, before the add).
+__device__ __forceinline__ int atom_add_release_gpu(int* addr, int v) {
+    int old;
+    asm volatile("atom.add.release.gpu.global.s32 %0, [%1], %2;"
+                 : "=r"(old) : "l"(addr), "r"(v) : "memory");
+    return old;
+}
+
 // Relaxed atomic add at GPU scope (ordering comes from fences around it).
 __device__ __forceinline__ int atom_add_relaxed_gpu(int* addr, int v) {
     int old;
