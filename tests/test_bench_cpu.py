@@ -68,3 +68,23 @@ def test_phase_trace_summary_separates_overlapping_launches():
     assert out["period_us_median"] == 1.0
     assert out["dep_wait"]["median_cta_us"] == pytest.approx(1.505)
     assert out["stored"]["latest_cta_us"] == pytest.approx(1.91)
+
+
+def test_phase_trace_reads_nonzero_records_in_time_order():
+    """The trace buffer is zeroed before a run: records_by_cta keeps the
+    non-empty records of each CTA, sorted by time, and drops idle CTAs."""
+    raw = np.zeros((3, 8), dtype=P.REC)
+    raw[0][[5, 1]] = [(300, 7, 4), (100, 7, 1)]     # written out of order
+    raw[2][[0]] = [(50, 9, 1)]
+    out = P.records_by_cta(raw)
+    assert sorted(out) == [0, 2]
+    assert list(out[0]["t"]) == [100, 300] and list(out[0]["launch"]) == [7, 7]
+    assert list(out[2]["ev_sm"]) == [1]
+
+
+def test_e2e_pipelines_only_per_layer_workloads():
+    """The end-to-end leg overlaps host copies with the calls only for
+    workloads that expose one call per layer; the paged workload (one call
+    per step) keeps the serial copies."""
+    assert callable(getattr(bench.Cfg3, "run_layer", None))
+    assert getattr(bench.Cfg3Paged, "run_layer", None) is None
